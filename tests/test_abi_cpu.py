@@ -1,0 +1,65 @@
+"""The C ABI library loads without a GPU, exports every declared entry point,
+and rejects bad arguments before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared(header):
+    text = open(os.path.join(ROOT, "include", header)).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"\b(tkb_[a-z0-9_]+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    import tokamak_b200
+    L = tokamak_b200.lib()
+    names = declared("tkm_b200.h")
+    assert len(names) >= 20, names
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert b"sm_100a" in L.tkb_version()
+
+
+def test_python_signatures_cover_header():
+    import tokamak_b200
+    assert set(declared("tkm_b200.h")) <= set(tokamak_b200._SIGS)
+
+
+def test_argument_errors_without_device():
+    import tokamak_b200
+    L = tokamak_b200.lib()
+    vp = ctypes.c_void_p
+    # head dim 96 is not supported: rejected before any CUDA call
+    rc = L.tkb_gqa_attn_fwd(vp(16), vp(16), vp(16), 1, 128, 2, 1, 96, 0.1, 1, 1, None)
+    assert rc == -3
+    assert b"head dim" in L.tkb_last_error()
+    # Hq not a multiple of Hkv
+    rc = L.tkb_gqa_attn_fwd(vp(16), vp(16), vp(16), 1, 128, 3, 2, 64, 0.1, 1, 1, None)
+    assert rc == -1
+    # odd channel count (the reference requires even C, src/tkm_core.c:341-345)
+    rc = L.tkb_add_rmsnorm_fwd(vp(16), None, None, vp(16), vp(16), None, 4, 7, 1e-5, 1, None)
+    assert rc == -1
+    # bad dtype
+    rc = L.tkb_softmax_fwd(vp(16), vp(16), 4, 8, 9, None)
+    assert rc == -1
+    # missing workspace
+    rc = L.tkb_softmax_loss(vp(16), None, None, vp(16), None, None, 0, 4, 8, 0, 2.0, 1, None)
+    assert rc == -4
+
+
+def test_workspace_sizes():
+    import tokamak_b200
+    L = tokamak_b200.lib()
+    # fp32 dQ sums + LSE + Delta for B*Hq*S_pad rows
+    n = L.tkb_gqa_attn_bwd_workspace(8, 4096, 16, 128, 1)
+    rows = 8 * 16 * 4096
+    assert n >= rows * 128 * 4 + 2 * rows * 4
+    assert L.tkb_gqa_attn_bwd_workspace(8, 4096, 16, 128, 0) == 0
+    assert L.tkb_add_rmsnorm_bwd_workspace(16384, 4096) > 0
+    assert L.tkb_softmax_loss_workspace(8192) >= 8192 * 4

@@ -1,0 +1,361 @@
+// attn_fwd.cu -- GQA flash-attention forward for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Replaces k_gqa_flash_attn_tc_fwd<HEAD_DIM> (src/tkm_gpu.cu:302-438 of the
+// reference), same semantics: O = softmax(Q K^T * scale, causal key>query
+// masked) V per head, LSE = ln(sum exp) per (b, q-head, row), kv head =
+// q head / (Hq/Hkv).
+//
+// One CTA owns two 128-row query tiles of one (batch, q-head) and streams the
+// 128-key K/V blocks of the matching kv head through shared memory.
+//   warps 0-3  softmax warpgroup for query tile 0 (thread = query row)
+//   warps 4-7  softmax warpgroup for query tile 1
+//   warp 8     TMA producer (Q once, K/V ring of NST stages)
+//   warp 9     tcgen05 MMA issuer, TMEM owner
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
+// The softmax warps overwrite the first 64 columns of S with P (16-bit pairs),
+// which the P*V MMA reads straight from TMEM.  Causal blocks above the
+// diagonal are never loaded or computed.
+#include "tkb_common.cuh"
+#include "tkb_internal.h"
+
+namespace tkb {
+
+template <int D>
+struct FwdCfg {
+  static constexpr int TILE = 128 * D * 2;  // bytes of one 128-row x D tile
+  static constexpr int SLAB = 128 * 128;    // bytes of one 64-column swizzle slab
+  static constexpr int NST = (D == 64) ? 4 : 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + 2 * TILE;
+  static constexpr int OFF_V = OFF_K + NST * TILE;
+  static constexpr int OFF_BAR = OFF_V + NST * TILE;
+  // q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST], s_full[2], p_ready[2], o_done[2], drain
+  static constexpr int NBAR = 1 + 4 * NST + 7;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
+  static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
+};
+
+TKB_DEVFN void wait_ld_dep(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                 "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                 "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]),
+                 "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
+  using C = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + C::NST;
+  uint64_t* v_full = k_empty + C::NST;
+  uint64_t* v_empty = v_full + C::NST;
+  uint64_t* s_full = v_empty + C::NST;
+  uint64_t* p_ready = s_full + 2;
+  uint64_t* o_done = p_ready + 2;
+  uint64_t* mma_drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int BH = p.B * p.Hq;
+  const int bh = blockIdx.x % BH;
+  const int t = p.n_pairs - 1 - static_cast<int>(blockIdx.x / BH);  // longest (causal) first
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int g = h / (p.Hq / p.Hkv);
+  const int nkv = (p.S + 127) >> 7;
+  int nb[2];
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    const int qt = 2 * t + w;
+    nb[w] = (qt * 128 >= p.S) ? 0 : (p.causal ? min(qt + 1, nkv) : nkv);
+  }
+  const int nblk = max(nb[0], nb[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&s_full[w], 1);
+      mbar_init(&p_ready[w], 128);
+      mbar_init(&o_done[w], 1);
+    }
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&p.tmQ);
+      prefetch_tmap(&p.tmK);
+      prefetch_tmap(&p.tmV);
+      const uint64_t pol_q = policy_evict_first(), pol_kv = policy_evict_last();
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE);
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh)
+          tma_load_3d(smem + C::OFF_Q + w * C::TILE + hh * C::SLAB, &p.tmQ, q_full, h * D + hh * 64,
+                      (2 * t + w) * 128, b, pol_q);
+      int issued = 0;
+      for (int j = 0; j < nblk; ++j) {
+        const int s = j % C::NST;
+        const uint32_t ph = (j / C::NST) & 1;
+        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[s], C::TILE);
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh)
+          tma_load_3d(smem + C::OFF_K + s * C::TILE + hh * C::SLAB, &p.tmK, &k_full[s], g * D + hh * 64,
+                      j * 128, b, pol_kv);
+        if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag)) {
+          issued = -(j + 1);  // K of block j is in flight, V is not
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[s], C::TILE);
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh)
+          tma_load_3d(smem + C::OFF_V + s * C::TILE + hh * C::SLAB, &p.tmV, &v_full[s], g * D + hh * 64,
+                      j * 128, b, pol_kv);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // Let every copy this CTA started land before the CTA exits.
+        volatile int never = 0;
+        mbar_wait(q_full, 0, &never);
+        const int nk = issued < 0 ? -issued : issued, nv = issued < 0 ? -issued - 1 : issued;
+        for (int j = max(0, nk - C::NST); j < nk; ++j) mbar_wait(&k_full[j % C::NST], (j / C::NST) & 1, &never);
+        for (int j = max(0, nv - C::NST); j < nv; ++j) mbar_wait(&v_full[j % C::NST], (j / C::NST) & 1, &never);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nblk > 0) {
+      constexpr uint32_t idS = idesc_f16kind(128, 128, BF16, false, false);
+      constexpr uint32_t idO = idesc_f16kind(128, D, BF16, false, true);
+      const uint32_t sQ = sbase + C::OFF_Q, sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      auto issue_S = [&](int w, int s) {
+        const uint32_t qa = sQ + w * C::TILE, ka = sK + s * C::TILE;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::SLAB + (kk & 3) * 32;
+          umma_ss(tmem + (w ? C::TM_S1 : C::TM_S0), sdesc_sw128(qa + off, 16, 1024),
+                  sdesc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_PV = [&](int w, int s, bool acc) {
+        const uint32_t va = sV + s * C::TILE;
+        const uint32_t tP = tmem + (w ? C::TM_S1 : C::TM_S0);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(tmem + (w ? C::TM_O1 : C::TM_O0), tP + kk * 8, sdesc_sw128(va + kk * 2048, C::SLAB, 1024), idO,
+                  (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int w = 0; w < 2; ++w)
+          if (nb[w] > 0) {
+            issue_S(w, 0);
+            umma_commit(&s_full[w]);
+          }
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int s = j % C::NST, s1 = (j + 1) % C::NST;
+        if (!(ok = mbar_wait(&v_full[s], (j / C::NST) & 1, abort_flag))) break;
+        bool k_next = false;
+        for (int w = 0; w < 2 && ok; ++w) {
+          if (j >= nb[w]) continue;
+          if (!(ok = mbar_wait(&p_ready[w], j & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_PV(w, s, j > 0);
+          if (j == nb[w] - 1) umma_commit(&o_done[w]);
+          if (j + 1 < nb[w]) {
+            if (!k_next) {
+              if (!(ok = mbar_wait(&k_full[s1], ((j + 1) / C::NST) & 1, abort_flag))) break;
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_S(w, s1);
+            umma_commit(&s_full[w]);
+          }
+        }
+        umma_commit(&v_empty[s]);
+        if (k_next) umma_commit(&k_empty[s1]);
+      }
+      if (!ok) {
+        // Make sure no MMA is still running when TMEM is released.
+        volatile int never = 0;
+        umma_commit(mma_drain);
+        mbar_wait(mma_drain, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups
+    const int w = warp >> 2;
+    const int r = threadIdx.x & 127;
+    const int qt = 2 * t + w;
+    const int qrow = qt * 128 + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + (w ? C::TM_S1 : C::TM_S0);
+    const uint32_t tO = tmem + lane_off + (w ? C::TM_O1 : C::TM_O0);
+    const float sl2 = p.scale_log2;
+    float m_used = 0.f, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nb[w]; ++j) {
+      if (!(ok = mbar_wait(&s_full[w], j & 1, abort_flag))) break;
+      tc_fence_after();
+      uint32_t r0[32], r1[32], r2[32], r3[32];
+      tmem_ld32(tS + 0, r0);
+      tmem_ld32(tS + 32, r1);
+      tmem_ld32(tS + 64, r2);
+      tmem_ld32(tS + 96, r3);
+      wait_ld_dep(r0);
+      wait_ld_dep(r1);
+      wait_ld_dep(r2);
+      wait_ld_dep(r3);
+      float sv[128];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        sv[i] = __uint_as_float(r0[i]);
+        sv[32 + i] = __uint_as_float(r1[i]);
+        sv[64 + i] = __uint_as_float(r2[i]);
+        sv[96 + i] = __uint_as_float(r3[i]);
+      }
+      const int kbase = j * 128;
+      if ((p.causal && kbase + 127 > qt * 128) || kbase + 128 > p.S) {
+        const int lim = min(p.S - kbase, p.causal ? qrow - kbase + 1 : 128);
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c >= lim) sv[c] = -INFINITY;
+      }
+      float mx0 = sv[0], mx1 = sv[1], mx2 = sv[2], mx3 = sv[3];
+#pragma unroll
+      for (int c = 4; c < 128; c += 4) {
+        mx0 = fmaxf(mx0, sv[c]);
+        mx1 = fmaxf(mx1, sv[c + 1]);
+        mx2 = fmaxf(mx2, sv[c + 2]);
+        mx3 = fmaxf(mx3, sv[c + 3]);
+      }
+      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      if (j == 0) {
+        m_used = (mx == -INFINITY) ? 0.f : mx;
+      } else if (mx > m_used + 8.0f) {
+        // Raise the running max: rescale the partial O row and the row sum.
+        const float f = ex2(m_used - mx);
+        l *= f;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          wait_ld_dep(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st32(tO + c * 32, o);
+        }
+        m_used = mx;
+      }
+      const float nm = -m_used;
+      uint32_t pk0[32], pk1[32];
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = ex2(fmaf(sv[2 * i], sl2, nm));
+        const float c = ex2(fmaf(sv[2 * i + 1], sl2, nm));
+        ls0 += a;
+        ls1 += c;
+        pk0[i] = pack2<BF16>(a, c);
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = ex2(fmaf(sv[64 + 2 * i], sl2, nm));
+        const float c = ex2(fmaf(sv[64 + 2 * i + 1], sl2, nm));
+        ls0 += a;
+        ls1 += c;
+        pk1[i] = pack2<BF16>(a, c);
+      }
+      l += ls0 + ls1;
+      tmem_st32(tS + 0, pk0);
+      tmem_st32(tS + 32, pk1);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[w]);
+    }
+    if (ok && nb[w] > 0 && mbar_wait(&o_done[w], 0, abort_flag)) {
+      tc_fence_after();
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+      const bool valid = qrow < p.S;
+      uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) +
+                      2 * (static_cast<long long>(b) * p.out_batch_stride +
+                           static_cast<long long>(qrow) * p.out_row_stride + static_cast<long long>(h) * D);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        wait_ld_dep(o);
+        uint4 v[4];
+        uint32_t* vw = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          vw[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l, __uint_as_float(o[2 * i + 1]) * inv_l);
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = v[i];
+        }
+      }
+      if (valid && p.lse)
+        p.lse[static_cast<long long>(bh) * p.S + qrow] = (m_used + lg2(l)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D, bool BF16>
+static cudaError_t launch_fwd(const FwdParams& p, cudaStream_t stream) {
+  using C = FwdCfg<D>;
+  auto kern = attn_fwd_tc_kernel<D, BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const unsigned grid = static_cast<unsigned>(p.B * p.Hq * p.n_pairs);
+  kern<<<grid, 320, C::SMEM, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t attn_fwd_tc(const FwdParams& p, int D, bool bf16, cudaStream_t stream) {
+  if (D == 128) return bf16 ? launch_fwd<128, true>(p, stream) : launch_fwd<128, false>(p, stream);
+  if (D == 64) return bf16 ? launch_fwd<64, true>(p, stream) : launch_fwd<64, false>(p, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tkb

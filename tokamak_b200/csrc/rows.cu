@@ -1,0 +1,868 @@
+// rows.cu -- HBM-bound fused row kernels of the hot path, for sm_100a.
+//
+// These replace the NVRTC "plasma group" kernels the reference emits from
+// src/tkm_codegen.c (RMSNorm group, twin SwiGLU epilogue, QKV-prep with RoPE)
+// and its static softmax / loss kernels (src/tkm_gpu.cu:600-682).  Design:
+//   * one 256-thread block per row (grid-stride over rows) for row reductions,
+//     the row kept in registers so HBM is read and written exactly once;
+//   * 16-byte vector accesses (8 x 16-bit or 2 x float4) when the row length
+//     allows, 2-element accesses otherwise (the reference requires even C);
+//   * block-wide reductions (warp shuffles + shared memory) over the full row;
+//   * column reductions for parameter gradients as per-block fp32 partials
+//     reduced by a second kernel (deterministic, no atomics).
+#include "tkb_common.cuh"
+
+namespace tkb {
+
+// ------------------------------------------------------------------ loads
+template <typename T>
+struct Elem;
+template <>
+struct Elem<float> {
+  static TKB_DEVFN float ld(const float* p) { return *p; }
+  static TKB_DEVFN void st(float* p, float v) { *p = v; }
+};
+template <>
+struct Elem<__nv_bfloat16> {
+  static TKB_DEVFN float ld(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static TKB_DEVFN void st(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+};
+template <>
+struct Elem<__half> {
+  static TKB_DEVFN float ld(const __half* p) { return __half2float(*p); }
+  static TKB_DEVFN void st(__half* p, float v) { *p = __float2half_rn(v); }
+};
+
+// VEC consecutive elements <-> floats.  VEC = 8 uses 16-byte transactions.
+template <typename T, int VEC>
+TKB_DEVFN void ldv(const T* p, float (&f)[VEC]) {
+  if constexpr (VEC == 8 && sizeof(T) == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 t;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) t = unpack2<true>(w[i]);
+      else t = unpack2<false>(w[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  } else if constexpr (VEC == 8 && sizeof(T) == 4) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = Elem<T>::ld(p + i);
+  }
+}
+template <typename T, int VEC>
+TKB_DEVFN void stv(T* p, const float (&f)[VEC]) {
+  if constexpr (VEC == 8 && sizeof(T) == 2) {
+    uint4 u;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      u.x = pack2<true>(f[0], f[1]); u.y = pack2<true>(f[2], f[3]);
+      u.z = pack2<true>(f[4], f[5]); u.w = pack2<true>(f[6], f[7]);
+    } else {
+      u.x = pack2<false>(f[0], f[1]); u.y = pack2<false>(f[2], f[3]);
+      u.z = pack2<false>(f[4], f[5]); u.w = pack2<false>(f[6], f[7]);
+    }
+    *reinterpret_cast<uint4*>(p) = u;
+  } else if constexpr (VEC == 8 && sizeof(T) == 4) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) Elem<T>::st(p + i, f[i]);
+  }
+}
+// Round a float through T (what a store followed by a load would give).
+template <typename T>
+TKB_DEVFN float rnd(float v) {
+  if constexpr (std::is_same<T, float>::value) return v;
+  else if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(v));
+  else return __half2float(__float2half_rn(v));
+}
+template <int VEC>
+TKB_DEVFN void ldf(const float* p, float (&f)[VEC]) {
+  if constexpr (VEC == 8) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = p[i];
+  }
+}
+
+constexpr int NT = 256;  // threads per row block
+
+TKB_DEVFN float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+TKB_DEVFN float warp_max(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+// Block-wide sum for NT threads; `sh` holds >= 32 floats; safe to call repeatedly.
+TKB_DEVFN float block_sum(float v, float* sh) {
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane_id() == 0) sh[warp_id()] = v;
+  __syncthreads();
+  float t = lane_id() < NT / 32 ? sh[lane_id()] : 0.f;
+  return warp_sum(t);
+}
+TKB_DEVFN float block_max(float v, float* sh) {
+  v = warp_max(v);
+  __syncthreads();
+  if (lane_id() == 0) sh[warp_id()] = v;
+  __syncthreads();
+  float t = lane_id() < NT / 32 ? sh[lane_id()] : -INFINITY;
+  return warp_max(t);
+}
+
+static int row_grid(int rows, int per_sm) {
+  const int cap = 148 * per_sm;
+  return rows < cap ? (rows < 1 ? 1 : rows) : cap;
+}
+
+// ============================================================ Add + RMSNorm
+// s = x + r, istd = 1/sqrt(mean(s^2) + eps), y = s * istd * gamma
+// (RMSNorm spec src/tkm_registry.c:228-238, Add spec 435-439).
+template <typename T, int VEC, int MAXV>
+__global__ void __launch_bounds__(NT) add_rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ r,
+                                                             T* __restrict__ s, T* __restrict__ y,
+                                                             const float* __restrict__ gamma,
+                                                             float* __restrict__ istd, int rows, int C, float eps) {
+  __shared__ float sh[32];
+  const int nvec = C / VEC;
+  const float invC = 1.0f / static_cast<float>(C);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * C;
+    float v[MAXV][VEC];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        ldv<T, VEC>(x + base + vi * VEC, v[i]);
+        if (r) {
+          float rr[VEC];
+          ldv<T, VEC>(r + base + vi * VEC, rr);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) v[i][e] = rnd<T>(v[i][e] + rr[e]);
+          if (s) stv<T, VEC>(s + base + vi * VEC, v[i]);
+        }
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) ss = fmaf(v[i][e], v[i][e], ss);
+      }
+    }
+    ss = block_sum(ss, sh);
+    const float is = 1.0f / sqrtf(ss * invC + eps);
+    if (threadIdx.x == 0 && istd) istd[row] = is;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        float g[VEC];
+        ldf<VEC>(gamma + vi * VEC, g);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[i][e] = v[i][e] * is * g[e];
+        stv<T, VEC>(y + base + vi * VEC, v[i]);
+      }
+    }
+  }
+}
+
+// dx = istd*(gamma*dy - xh*mean(gamma*dy*xh)) + ds_skip, xh = s*istd;
+// dgamma partial per block = sum over its rows of dy*xh   (src/tkm_registry.c:239-245).
+template <typename T, int VEC, int MAXV>
+__global__ void __launch_bounds__(NT) add_rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ s,
+                                                             const float* __restrict__ gamma,
+                                                             const float* __restrict__ istd,
+                                                             const T* __restrict__ ds_skip, T* __restrict__ dx,
+                                                             float* __restrict__ partial, int rows, int C) {
+  __shared__ float sh[32];
+  const int nvec = C / VEC;
+  const float invC = 1.0f / static_cast<float>(C);
+  float g[MAXV][VEC], dg[MAXV][VEC];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int vi = threadIdx.x + i * NT;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) dg[i][e] = 0.f;
+    if (vi < nvec) ldf<VEC>(gamma + vi * VEC, g[i]);
+  }
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * C;
+    const float is = istd[row];
+    float d[MAXV][VEC], xh[MAXV][VEC];
+    float m2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        ldv<T, VEC>(dy + base + vi * VEC, d[i]);
+        ldv<T, VEC>(s + base + vi * VEC, xh[i]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          xh[i][e] *= is;
+          m2 = fmaf(d[i][e] * g[i][e], xh[i][e], m2);
+          dg[i][e] = fmaf(d[i][e], xh[i][e], dg[i][e]);
+        }
+      }
+    }
+    m2 = block_sum(m2, sh) * invC;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        float o[VEC];
+        if (ds_skip) ldv<T, VEC>(ds_skip + base + vi * VEC, o);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float v = is * (d[i][e] * g[i][e] - xh[i][e] * m2);
+          o[e] = ds_skip ? o[e] + v : v;
+        }
+        stv<T, VEC>(dx + base + vi * VEC, o);
+      }
+    }
+  }
+  if (partial) {
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        float* pp = partial + static_cast<long long>(blockIdx.x) * C + vi * VEC;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) pp[e] = dg[i][e];
+      }
+    }
+  }
+}
+
+// out[c] += sum_b partial[b][c]  (fixed order: deterministic)
+__global__ void __launch_bounds__(256) column_reduce_kernel(const float* __restrict__ partial, int nblk, int C,
+                                                            float* __restrict__ out0, float* __restrict__ out1,
+                                                            int split) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float acc = 0.f;
+  for (int b = 0; b < nblk; ++b) acc += partial[static_cast<long long>(b) * C + c];
+  if (c < split) {
+    if (out0) out0[c] += acc;
+  } else {
+    if (out1) out1[c - split] += acc;
+  }
+}
+
+// ============================================================ SwiGLU twin epilogue
+// gu [rows][2F] (gate | up), h = silu(g + bg) * (u + bu)
+// (src/tkm_codegen.c:511-518; SiLU spec src/tkm_registry.c:272-278)
+TKB_DEVFN float sigmoidf_(float a) { return 1.0f / (1.0f + expf(-a)); }
+
+// Block (bx, by): columns [bx*NT*VEC, ...), rows by, by+gridDim.y, ...
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) swiglu_fwd_kernel(const T* __restrict__ gu, const float* __restrict__ bg,
+                                                        const float* __restrict__ bu, T* __restrict__ h, int rows,
+                                                        int F) {
+  const int c0 = (blockIdx.x * NT + threadIdx.x) * VEC;
+  if (c0 >= F) return;
+  float b1[VEC], b2[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) { b1[e] = 0.f; b2[e] = 0.f; }
+  if (bg) ldf<VEC>(bg + c0, b1);
+  if (bu) ldf<VEC>(bu + c0, b2);
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const long long gb = static_cast<long long>(row) * 2 * F;
+    float a[VEC], u[VEC], o[VEC];
+    ldv<T, VEC>(gu + gb + c0, a);
+    ldv<T, VEC>(gu + gb + F + c0, u);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float av = a[e] + b1[e];
+      o[e] = av * sigmoidf_(av) * (u[e] + b2[e]);
+    }
+    stv<T, VEC>(h + static_cast<long long>(row) * F + c0, o);
+  }
+}
+
+// dg = dh*b*sig(a)*(1 + a*(1 - sig(a))), du = dh*silu(a)  (src/tkm_registry.c:275-277, codegen 592-597)
+template <typename T, int VEC>
+__global__ void __launch_bounds__(NT) swiglu_bwd_kernel(const T* __restrict__ dh, const T* __restrict__ gu,
+                                                        const float* __restrict__ bg, const float* __restrict__ bu,
+                                                        T* __restrict__ dgu, float* __restrict__ partial, int rows,
+                                                        int F) {
+  const int c0 = (blockIdx.x * NT + threadIdx.x) * VEC;
+  if (c0 >= F) return;
+  float b1[VEC], b2[VEC], sg[VEC], su[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) { b1[e] = 0.f; b2[e] = 0.f; sg[e] = 0.f; su[e] = 0.f; }
+  if (bg) ldf<VEC>(bg + c0, b1);
+  if (bu) ldf<VEC>(bu + c0, b2);
+  for (int row = blockIdx.y; row < rows; row += gridDim.y) {
+    const long long gb = static_cast<long long>(row) * 2 * F;
+    float a[VEC], u[VEC], d[VEC], og[VEC], ou[VEC];
+    ldv<T, VEC>(gu + gb + c0, a);
+    ldv<T, VEC>(gu + gb + F + c0, u);
+    ldv<T, VEC>(dh + static_cast<long long>(row) * F + c0, d);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float av = a[e] + b1[e], bv = u[e] + b2[e];
+      const float sgm = sigmoidf_(av);
+      og[e] = d[e] * bv * sgm * (1.0f + av * (1.0f - sgm));
+      ou[e] = d[e] * av * sgm;
+      sg[e] += og[e];
+      su[e] += ou[e];
+    }
+    stv<T, VEC>(dgu + gb + c0, og);
+    stv<T, VEC>(dgu + gb + F + c0, ou);
+  }
+  if (partial) {
+    float* pp = partial + static_cast<long long>(blockIdx.y) * 2 * F;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      pp[c0 + e] = sg[e];
+      pp[F + c0 + e] = su[e];
+    }
+  }
+}
+
+// ============================================================ QKV prep (bias + QKNorm + RoPE)
+// src/tkm_codegen.c:211-295 with the rotation of 43-70.  One block per row
+// (grid-stride), threads over 8-column vectors; a vector never straddles a head.
+struct RopeTable {
+  double inv_freq[64];  // per pair index within a head (D/2 <= 64)
+};
+
+TKB_DEVFN void rope_cs(int pos, double invf, float& sn, float& cs) {
+  double a = static_cast<double>(pos) * invf;
+  a -= 6.283185307179586 * floor(a * 0.15915494309189535);
+  sincosf(static_cast<float>(a), &sn, &cs);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT) qkv_prep_fwd_kernel(const T* __restrict__ in, const float* __restrict__ bias,
+                                                          const float* __restrict__ gain, T* __restrict__ out,
+                                                          float* __restrict__ save_istd, int rows, int S, int Hq,
+                                                          int Hkv, int D, int has_qknorm, int has_rope,
+                                                          const RopeTable tab) {
+  const int C = (Hq + 2 * Hkv) * D, nqk = Hq + Hkv, nvec = C / 8;
+  const int grp = D / 8;  // threads per head
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const int pos = row % S;
+    const long long base = static_cast<long long>(row) * C;
+    for (int v0 = 0; v0 < nvec; v0 += NT) {
+      const int vi = v0 + threadIdx.x;
+      const bool act = vi < nvec;
+      const int c = vi * 8, hd = c / D;
+      float v[8];
+      if (act) {
+        ldv<T, 8>(in + base + c, v);
+        if (bias) {
+          float bb[8];
+          ldf<8>(bias + c, bb);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] += bb[e];
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      }
+      if (has_qknorm) {
+        // heads are aligned to groups of `grp` consecutive lanes (D/8 divides 32 or equals 16)
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(v[e], v[e], ss);
+        for (int m = grp >> 1; m >= 1; m >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, m);
+        if (act && hd < nqk) {
+          const float is = 1.0f / sqrtf(ss / static_cast<float>(D) + 1e-5f);
+          if (save_istd && (c % D) == 0) save_istd[static_cast<long long>(row) * nqk + hd] = is;
+          float gg[8];
+          if (gain) ldf<8>(gain + c, gg);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = v[e] * is * (gain ? gg[e] : 1.0f);
+        }
+      }
+      if (act && has_rope && hd < nqk) {
+        const int pi0 = (c % D) >> 1;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float sn, cs;
+          rope_cs(pos, tab.inv_freq[pi0 + e], sn, cs);
+          const float x0 = v[2 * e], x1 = v[2 * e + 1];
+          v[2 * e] = x0 * cs - x1 * sn;
+          v[2 * e + 1] = x0 * sn + x1 * cs;
+        }
+      }
+      if (act) stv<T, 8>(out + base + c, v);
+    }
+  }
+}
+
+// din += J^T dout; dbias partial, dgain partial per block.
+template <typename T>
+__global__ void __launch_bounds__(NT) qkv_prep_bwd_kernel(const T* __restrict__ dout, const T* __restrict__ in,
+                                                          const float* __restrict__ bias,
+                                                          const float* __restrict__ gain,
+                                                          const float* __restrict__ save_istd, T* __restrict__ din,
+                                                          float* __restrict__ partial, int rows, int S, int Hq,
+                                                          int Hkv, int D, int has_qknorm, int has_rope,
+                                                          const RopeTable tab) {
+  const int C = (Hq + 2 * Hkv) * D, nqk = Hq + Hkv, nvec = C / 8;
+  const int grp = D / 8;
+  // partial layout per block: [dbias C][dgain nqk*D]
+  const long long pstride = static_cast<long long>(C) + static_cast<long long>(nqk) * D;
+  for (int v0 = 0; v0 < nvec; v0 += NT) {
+    const int vi = v0 + threadIdx.x;
+    const bool act = vi < nvec;
+    const int c = vi * 8, hd = c / D;
+    float accb[8], accg[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { accb[e] = 0.f; accg[e] = 0.f; }
+    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+      const int pos = row % S;
+      const long long base = static_cast<long long>(row) * C;
+      float dy[8];
+      if (act) ldv<T, 8>(dout + base + c, dy);
+      else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dy[e] = 0.f;
+      }
+      if (act && has_rope && hd < nqk) {
+        const int pi0 = (c % D) >> 1;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float sn, cs;
+          rope_cs(pos, tab.inv_freq[pi0 + e], sn, cs);
+          const float y0 = dy[2 * e], y1 = dy[2 * e + 1];
+          dy[2 * e] = y0 * cs + y1 * sn;
+          dy[2 * e + 1] = -y0 * sn + y1 * cs;
+        }
+      }
+      if (has_qknorm) {
+        float xh[8], gg[8], m2 = 0.f;
+        float is = 0.f;
+        if (act && hd < nqk) {
+          is = save_istd[static_cast<long long>(row) * nqk + hd];
+          ldv<T, 8>(in + base + c, xh);
+          float bb[8];
+          if (bias) ldf<8>(bias + c, bb);
+          if (gain) ldf<8>(gain + c, gg);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            xh[e] = (xh[e] + (bias ? bb[e] : 0.f)) * is;
+            if (!gain) gg[e] = 1.f;
+            accg[e] = fmaf(dy[e], xh[e], accg[e]);
+            m2 = fmaf(dy[e] * gg[e], xh[e], m2);
+          }
+        }
+        for (int m = grp >> 1; m >= 1; m >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, m);
+        if (act && hd < nqk) {
+          m2 /= static_cast<float>(D);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dy[e] = is * (dy[e] * gg[e] - xh[e] * m2);
+        }
+      }
+      if (act) {
+        float prev[8];
+        ldv<T, 8>(din + base + c, prev);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          accb[e] += dy[e];
+          prev[e] += dy[e];
+        }
+        stv<T, 8>(din + base + c, prev);
+      }
+    }
+    if (act && partial) {
+      float* pp = partial + static_cast<long long>(blockIdx.x) * pstride;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pp[c + e] = accb[e];
+      if (hd < nqk) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) pp[C + c + e] = accg[e];
+      }
+    }
+  }
+}
+
+// ============================================================ softmax and softmax losses
+// Row kept in registers: MAXV vectors of VEC per thread (C <= NT*VEC*MAXV).
+template <typename T, int VEC, int MAXV>
+__global__ void __launch_bounds__(NT) softmax_fwd_kernel(const T* __restrict__ x, T* __restrict__ p, int rows, int C) {
+  __shared__ float sh[32];
+  const int nvec = C / VEC;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * C;
+    float v[MAXV][VEC];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        ldv<T, VEC>(x + base + vi * VEC, v[i]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) mx = fmaxf(mx, v[i][e]);
+      }
+    }
+    mx = block_max(mx, sh);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          v[i][e] = expf(v[i][e] - mx);
+          sum += v[i][e];
+        }
+      }
+    }
+    const float inv = 1.0f / block_sum(sum, sh);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[i][e] *= inv;
+        stv<T, VEC>(p + base + vi * VEC, v[i]);
+      }
+    }
+  }
+}
+
+// dx += p * (dp - <p, dp>)   (src/tkm_gpu.cu:615-630)
+template <typename T, int VEC, int MAXV>
+__global__ void __launch_bounds__(NT) softmax_bwd_kernel(const T* __restrict__ p, const T* __restrict__ dp,
+                                                         T* __restrict__ dx, int rows, int C) {
+  __shared__ float sh[32];
+  const int nvec = C / VEC;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * C;
+    float pv[MAXV][VEC], dv[MAXV][VEC];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        ldv<T, VEC>(p + base + vi * VEC, pv[i]);
+        ldv<T, VEC>(dp + base + vi * VEC, dv[i]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) dot = fmaf(pv[i][e], dv[i][e], dot);
+      }
+    }
+    dot = block_sum(dot, sh);
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        float o[VEC];
+        ldv<T, VEC>(dx + base + vi * VEC, o);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] += pv[i][e] * (dv[i][e] - dot);
+        stv<T, VEC>(dx + base + vi * VEC, o);
+      }
+    }
+  }
+}
+
+// Fused softmax loss forward + backward for one row per block
+// (src/tkm_gpu.cu:632-682): kind 0 CE, 1 focal(gamma), 2 Brier.
+// row_loss[row] receives the row's loss contribution already divided by rows.
+template <typename T, int VEC, int MAXV>
+__global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ logits,
+                                                          const int32_t* __restrict__ labels, T* __restrict__ dlogits,
+                                                          float* __restrict__ row_loss, int* __restrict__ correct,
+                                                          int rows, int C, int kind, float gamma) {
+  __shared__ float sh[32];
+  __shared__ int shi[32];
+  const int nvec = C / VEC;
+  const float inv_rows = 1.0f / static_cast<float>(rows);
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * C;
+    const int y = labels ? labels[row] : 0;
+    float v[MAXV][VEC];
+    float mx = -INFINITY;
+    int arg = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+        ldv<T, VEC>(logits + base + vi * VEC, v[i]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (v[i][e] > mx) { mx = v[i][e]; arg = vi * VEC + e; }
+      }
+    }
+    // (max, first index) reduction
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, mx, m);
+      const int oa = __shfl_xor_sync(0xffffffffu, arg, m);
+      if (om > mx || (om == mx && oa < arg)) { mx = om; arg = oa; }
+    }
+    __syncthreads();
+    if (lane_id() == 0) { sh[warp_id()] = mx; shi[warp_id()] = arg; }
+    __syncthreads();
+    mx = lane_id() < NT / 32 ? sh[lane_id()] : -INFINITY;
+    arg = lane_id() < NT / 32 ? shi[lane_id()] : 0x7fffffff;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, mx, m);
+      const int oa = __shfl_xor_sync(0xffffffffu, arg, m);
+      if (om > mx || (om == mx && oa < arg)) { mx = om; arg = oa; }
+    }
+    float sum = 0.f, xy = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = threadIdx.x + i * NT;
+      if (vi < nvec) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          if (vi * VEC + e == y) xy = v[i][e];
+          v[i][e] = expf(v[i][e] - mx);
+          sum += v[i][e];
+        }
+      }
+    }
+    sum = block_sum(sum, sh);
+    xy = block_sum(xy, sh);  // exactly one thread holds the label logit
+    const float inv_sum = 1.0f / sum;
+    float pt = expf(xy - mx) * inv_sum;
+    pt = fmaxf(pt, 1e-7f);
+    const float fw = powf(1.0f - pt, gamma);
+    const float fgs = kind == 1 ? fw - gamma * pt * powf(1.0f - pt, gamma - 1.0f) * logf(pt) : 1.0f;
+    float bdot = 0.f, brier = 0.f;
+    if (kind == 2) {
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = threadIdx.x + i * NT;
+        if (vi < nvec) {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float pc = v[i][e] * inv_sum, t = (vi * VEC + e == y) ? 1.f : 0.f;
+            bdot += pc * (pc - t);
+            brier += (pc - t) * (pc - t);
+          }
+        }
+      }
+      bdot = block_sum(bdot, sh);
+      brier = block_sum(brier, sh);
+    }
+    if (threadIdx.x == 0) {
+      float lr;
+      if (kind == 0) lr = -logf(pt) * inv_rows;
+      else if (kind == 1) lr = -fw * logf(pt) * inv_rows;
+      else lr = brier / static_cast<float>(C) * inv_rows;
+      if (row_loss) row_loss[row] = lr;
+      if (correct && arg == y) atomicAdd(correct, 1);
+    }
+    if (dlogits) {
+      const float k2 = 2.0f / static_cast<float>(C);
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        const int vi = threadIdx.x + i * NT;
+        if (vi < nvec) {
+          float o[VEC];
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float pc = v[i][e] * inv_sum, t = (vi * VEC + e == y) ? 1.f : 0.f;
+            float gr;
+            if (kind == 0) gr = pc - t;
+            else if (kind == 1) gr = fgs * (pc - t);
+            else gr = k2 * pc * ((pc - t) - bdot);
+            o[e] = gr * inv_rows;
+          }
+          stv<T, VEC>(dlogits + base + vi * VEC, o);
+        }
+      }
+    }
+  }
+}
+
+// loss += sum(row_loss) in a fixed order (one block).
+__global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ row_loss, int rows,
+                                                       float* __restrict__ loss) {
+  __shared__ float sh[32];
+  float acc = 0.f;
+  for (int r = threadIdx.x; r < rows; r += 256) acc += row_loss[r];
+  acc = block_sum(acc, sh);
+  if (threadIdx.x == 0) *loss += acc;
+}
+
+// ============================================================ multi-tensor SGD
+// src/tkm_gpu.cu:684-720: g += wd*p (tensors flagged for decay), v = m*v + g,
+// p -= lr*(m*v + g), refresh the 16-bit copy, bump the step seed.
+struct SgdTensor {
+  float* master;
+  float* vel;
+  const float* grad;
+  void* lowp;        // optional 16-bit copy (bf16 or f16 by lowp_dtype)
+  long long n;
+  int apply_wd;
+  int lowp_dtype;    // 1 = bf16, 2 = f16
+};
+
+__global__ void __launch_bounds__(256) sgd_kernel(const SgdTensor* __restrict__ tensors, int ntensors,
+                                                  const float* __restrict__ d_lr, float momentum, float wd,
+                                                  uint32_t* __restrict__ d_seed) {
+  const float lr = *d_lr;
+  for (int t = blockIdx.y; t < ntensors; t += gridDim.y) {
+    const SgdTensor T = tensors[t];
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < T.n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      float p = T.master[i];
+      float g = T.grad[i];
+      if (T.apply_wd) g = fmaf(wd, p, g);
+      const float v = fmaf(momentum, T.vel[i], g);
+      p = fmaf(-lr, fmaf(momentum, v, g), p);
+      T.vel[i] = v;
+      T.master[i] = p;
+      if (T.lowp) {
+        if (T.lowp_dtype == 1) reinterpret_cast<__nv_bfloat16*>(T.lowp)[i] = __float2bfloat16_rn(p);
+        else reinterpret_cast<__half*>(T.lowp)[i] = __float2half_rn(p);
+      }
+    }
+  }
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && d_seed) *d_seed += 0x9E3779B9u;
+}
+
+// ============================================================ dispatch
+#define TKB_ROW_DISPATCH(KERNEL, T, VEC, C, GRID, ST, ...)                                    \
+  do {                                                                                        \
+    const int _nv = ((C) / (VEC) + NT - 1) / NT;                                              \
+    if (_nv <= 1) KERNEL<T, VEC, 1><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                        \
+    else if (_nv <= 2) KERNEL<T, VEC, 2><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                   \
+    else if (_nv <= 4) KERNEL<T, VEC, 4><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                   \
+    else if (_nv <= 8) KERNEL<T, VEC, 8><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                   \
+    else if (_nv <= 16) KERNEL<T, VEC, 16><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                 \
+    else return cudaErrorInvalidValue;                                                        \
+  } while (0)
+
+template <typename T>
+static cudaError_t add_rmsnorm_fwd_t(const void* x, const void* r, void* s, void* y, const float* gamma, float* istd,
+                                     int rows, int C, float eps, cudaStream_t st) {
+  const int grid = row_grid(rows, 8);
+  if (C % 8 == 0)
+    TKB_ROW_DISPATCH(add_rmsnorm_fwd_kernel, T, 8, C, grid, st, (const T*)x, (const T*)r, (T*)s, (T*)y, gamma, istd,
+                     rows, C, eps);
+  else
+    TKB_ROW_DISPATCH(add_rmsnorm_fwd_kernel, T, 2, C, grid, st, (const T*)x, (const T*)r, (T*)s, (T*)y, gamma, istd,
+                     rows, C, eps);
+  return cudaGetLastError();
+}
+
+int add_rmsnorm_bwd_grid(int rows) { return row_grid(rows, 4); }
+
+template <typename T>
+static cudaError_t add_rmsnorm_bwd_t(const void* dy, const void* s, const float* gamma, const float* istd,
+                                     const void* ds_skip, void* dx, float* dgamma, float* partial, int rows, int C,
+                                     cudaStream_t st) {
+  const int grid = add_rmsnorm_bwd_grid(rows);
+  float* part = dgamma ? partial : nullptr;
+  if (C % 8 == 0)
+    TKB_ROW_DISPATCH(add_rmsnorm_bwd_kernel, T, 8, C, grid, st, (const T*)dy, (const T*)s, gamma, istd,
+                     (const T*)ds_skip, (T*)dx, part, rows, C);
+  else
+    TKB_ROW_DISPATCH(add_rmsnorm_bwd_kernel, T, 2, C, grid, st, (const T*)dy, (const T*)s, gamma, istd,
+                     (const T*)ds_skip, (T*)dx, part, rows, C);
+  if (dgamma) column_reduce_kernel<<<(C + 255) / 256, 256, 0, st>>>(partial, grid, C, dgamma, nullptr, C);
+  return cudaGetLastError();
+}
+
+// SwiGLU grid: x covers columns, y covers row slices.
+void swiglu_grid(int rows, int F, int vec, int& gx, int& gy) {
+  gx = (F / vec + NT - 1) / NT;
+  int want = (148 * 8 + gx - 1) / gx;
+  gy = rows < want ? rows : want;
+  if (gy < 1) gy = 1;
+}
+
+template <typename T>
+static cudaError_t swiglu_fwd_t(const void* gu, const float* bg, const float* bu, void* h, int rows, int F,
+                                cudaStream_t st) {
+  const int vec = (F % 8 == 0) ? 8 : 2;
+  int gx, gy;
+  swiglu_grid(rows, F, vec, gx, gy);
+  if (vec == 8) swiglu_fwd_kernel<T, 8><<<dim3(gx, gy), NT, 0, st>>>((const T*)gu, bg, bu, (T*)h, rows, F);
+  else swiglu_fwd_kernel<T, 2><<<dim3(gx, gy), NT, 0, st>>>((const T*)gu, bg, bu, (T*)h, rows, F);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t swiglu_bwd_t(const void* dh, const void* gu, const float* bg, const float* bu, void* dgu,
+                                float* dbg, float* dbu, float* partial, int rows, int F, cudaStream_t st) {
+  const int vec = (F % 8 == 0) ? 8 : 2;
+  int gx, gy;
+  swiglu_grid(rows, F, vec, gx, gy);
+  float* part = (dbg || dbu) ? partial : nullptr;
+  if (vec == 8)
+    swiglu_bwd_kernel<T, 8><<<dim3(gx, gy), NT, 0, st>>>((const T*)dh, (const T*)gu, bg, bu, (T*)dgu, part, rows, F);
+  else
+    swiglu_bwd_kernel<T, 2><<<dim3(gx, gy), NT, 0, st>>>((const T*)dh, (const T*)gu, bg, bu, (T*)dgu, part, rows, F);
+  if (part) column_reduce_kernel<<<(2 * F + 255) / 256, 256, 0, st>>>(part, gy, 2 * F, dbg, dbu, F);
+  return cudaGetLastError();
+}
+
+int qkv_prep_bwd_grid(int rows) { return row_grid(rows, 4); }
+
+template <typename T>
+static cudaError_t qkv_prep_fwd_t(const void* in, const float* bias, const float* gain, void* out, float* save_istd,
+                                  int rows, int S, int Hq, int Hkv, int D, int qkn, int rope, const RopeTable& tab,
+                                  cudaStream_t st) {
+  qkv_prep_fwd_kernel<T><<<row_grid(rows, 8), NT, 0, st>>>((const T*)in, bias, gain, (T*)out, save_istd, rows, S, Hq,
+                                                          Hkv, D, qkn, rope, tab);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t qkv_prep_bwd_t(const void* dout, const void* in, const float* bias, const float* gain,
+                                  const float* save_istd, void* din, float* dbias, float* dgain, float* partial,
+                                  int rows, int S, int Hq, int Hkv, int D, int qkn, int rope, const RopeTable& tab,
+                                  cudaStream_t st) {
+  const int grid = qkv_prep_bwd_grid(rows);
+  const bool want = dbias || (qkn && dgain);
+  qkv_prep_bwd_kernel<T><<<grid, NT, 0, st>>>((const T*)dout, (const T*)in, bias, gain, save_istd, (T*)din,
+                                             want ? partial : nullptr, rows, S, Hq, Hkv, D, qkn, rope, tab);
+  if (want) {
+    const int C = (Hq + 2 * Hkv) * D, G = (Hq + Hkv) * D;
+    const int tot = C + G;
+    column_reduce_kernel<<<(tot + 255) / 256, 256, 0, st>>>(partial, grid, tot, dbias, qkn ? dgain : nullptr, C);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t softmax_fwd_t(const void* x, void* p, int rows, int C, cudaStream_t st) {
+  const int grid = row_grid(rows, 8);
+  if (C % 8 == 0) TKB_ROW_DISPATCH(softmax_fwd_kernel, T, 8, C, grid, st, (const T*)x, (T*)p, rows, C);
+  else TKB_ROW_DISPATCH(softmax_fwd_kernel, T, 2, C, grid, st, (const T*)x, (T*)p, rows, C);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t softmax_bwd_t(const void* p, const void* dp, void* dx, int rows, int C, cudaStream_t st) {
+  const int grid = row_grid(rows, 8);
+  if (C % 8 == 0) TKB_ROW_DISPATCH(softmax_bwd_kernel, T, 8, C, grid, st, (const T*)p, (const T*)dp, (T*)dx, rows, C);
+  else TKB_ROW_DISPATCH(softmax_bwd_kernel, T, 2, C, grid, st, (const T*)p, (const T*)dp, (T*)dx, rows, C);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t softmax_loss_t(const void* logits, const int32_t* labels, void* dlogits, float* loss, int* correct,
+                                  float* row_loss, int rows, int C, int kind, float gamma, cudaStream_t st) {
+  const int grid = row_grid(rows, 8);
+  if (C % 8 == 0)
+    TKB_ROW_DISPATCH(softmax_loss_kernel, T, 8, C, grid, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
+                     rows, C, kind, gamma);
+  else
+    TKB_ROW_DISPATCH(softmax_loss_kernel, T, 2, C, grid, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
+                     rows, C, kind, gamma);
+  if (loss) sum_rows_kernel<<<1, 256, 0, st>>>(row_loss, rows, loss);
+  return cudaGetLastError();
+}
+
+}  // namespace tkb
