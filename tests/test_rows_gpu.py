@@ -107,7 +107,8 @@ def test_qkv_prep(rng, dtype, qknorm, rope, scale, Hq, Hkv, D):
                    dbias=db, dgain=dgn if qknorm else None)
     rdin, rdb, rdg = oracle.qkv_prep_bwd(doutn, xn, b.cpu().numpy(), gq.cpu().numpy() if qknorm else None,
                                          ristd, S, Hq, Hkv, D, qknorm, rope, **okw)
-    assert rel_l2(din.float().cpu().numpy() - din0n, rdin) < tol(dtype) * (3 if dtype != torch.float32 else 1)
+    # din is accumulated in place: compare the stored result with din0 + J^T dout
+    assert rel_l2(din.float().cpu().numpy(), din0n + rdin) < tol(dtype)
     assert rel_l2(db.cpu().numpy(), rdb) < tol(dtype)
     if qknorm:
         assert rel_l2(dgn.cpu().numpy(), rdg) < tol(dtype)
@@ -126,7 +127,8 @@ def test_softmax(rng, dtype, rows, C):
     dx = dx0.clone()
     o.softmax_bwd(p, dp, dx)
     rdx = oracle.softmax_bwd(p.float().cpu().numpy(), dpn, dx0n)
-    assert rel_l2(dx.float().cpu().numpy() - dx0n, rdx - dx0n) < tol(dtype) * (3 if dtype != torch.float32 else 1)
+    # dx is accumulated in place (dx += p*(dp - <p,dp>)): compare the stored result
+    assert rel_l2(dx.float().cpu().numpy(), rdx) < tol(dtype)
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
