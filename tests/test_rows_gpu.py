@@ -143,7 +143,13 @@ def test_softmax_loss(rng, dtype, kind, rows, C):
     loss, dl, corr = o.softmax_loss(x, tl, kind, 2.0)
     rloss, rdl, rcorr = oracle.softmax_loss(xn, lab, kind, 2.0)
     assert abs(loss.item() - rloss) <= 1e-5 + (1e-5 if dtype == torch.float32 else 1e-2) * abs(rloss)
-    assert rel_l2(dl.float().cpu().numpy(), rdl) < tol(dtype)
+    got = dl.float().cpu().numpy()
+    if dtype == torch.float16 and kind == 2:
+        # Brier gradients are O(1/(C*rows)) and fall into fp16's subnormal range:
+        # compare at fp16 resolution instead of relatively
+        assert np.abs(got - rdl).max() <= 1e-7 + 1e-2 * np.abs(rdl).max()
+    else:
+        assert rel_l2(got, rdl) < tol(dtype)
     assert corr.item() == rcorr
 
 
