@@ -150,6 +150,19 @@ int tkb_softmax_loss(const void *logits, const int32_t *labels, void *dlogits,
                      float *loss, int *correct, void *workspace, size_t workspace_bytes,
                      int rows, int C, int kind, float gamma, int dtype, void *stream);
 
+/* Variant of tkb_softmax_loss for callers that cannot allocate device memory
+ * (no counterpart in the reference).  Code running while a CUDA graph is being
+ * captured in global mode cannot call cudaMalloc, and foreign-language callers
+ * may hold only raw device pointers from another framework's allocator; this
+ * entry point needs no workspace.  Its per-row scratch is a fixed array inside
+ * the library (1 MiB per GPU, held until exit), so rows must be at most
+ * 262144; larger calls return TKB_ERR_ARG.  The first call on a device looks up
+ * the array's address for that device: make it before any stream capture.
+ * All calls share the array; calls that overlap on the GPU race on it. */
+int tkb_softmax_loss_noalloc(const void *logits, const int32_t *labels, void *dlogits,
+                             float *loss, int *correct, int rows, int C, int kind, float gamma,
+                             int dtype, void *stream);
+
 /* ------------------------------------------------------------ SGD
  * Replaces k_tkm_multi_tensor_sgd (src/tkm_gpu.cu:684-720, launch
  * 1417-1420).  `table` is device memory holding n_tensors tkb_sgd_tensor

@@ -48,6 +48,7 @@ _SIGS = {
     "tkb_softmax_bwd": ([_vp, _vp, _vp, _i, _i, _i, _vp], _i),
     "tkb_softmax_loss_workspace": ([_i], _sz),
     "tkb_softmax_loss": ([_vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _f, _i, _vp], _i),
+    "tkb_softmax_loss_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp], _i),
     "tkb_sgd_step": ([_vp, _i, _vp, _f, _f, _vp, _vp], _i),
 }
 

@@ -7,3 +7,4 @@
 #include "rows.cu"
 #include "capi.cu"
 #include "capi_rows.cu"
+#include "noalloc.cu"
