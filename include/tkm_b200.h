@@ -60,7 +60,7 @@ int tkb_gqa_attn_fwd(const void *qkv, void *out, float *lse,
                      int B, int S, int Hq, int Hkv, int D, float scale, int causal,
                      int dtype, void *stream);
 
-/* Workspace bytes tkb_gqa_attn_bwd needs (fp32 dQ sums, Delta, LSE copies). */
+/* Workspace bytes tkb_gqa_attn_bwd needs (per-row Delta and LSE*log2(e), fp32). */
 size_t tkb_gqa_attn_bwd_workspace(int B, int S, int Hq, int D, int dtype);
 
 /* Replaces k_gqa_flash_attn_tc_bwd<HEAD_DIM> (src/tkm_gpu.cu:440-598),

@@ -1,9 +1,8 @@
 // attn_aux.cu -- helpers around the tcgen05 attention kernels:
 //   * tensor-map construction (driver entry point fetched through the runtime,
 //     so the library never links libcuda directly),
-//   * the backward preprocess (Delta = rowsum(O*dO), LSE in log2 units,
-//     zeroing of the fp32 dQ accumulator),
-//   * the backward postprocess (fp32 dQ sums -> 16-bit dQ slice).
+//   * the backward preprocess (Delta = rowsum(O*dO), LSE in log2 units, both
+//     padded to a multiple of 128 rows per head).
 #include "tkb_common.cuh"
 #include "tkb_internal.h"
 
@@ -47,8 +46,7 @@ cudaError_t make_tmap_rows(CUtensorMap* m, const void* base, bool bf16, long lon
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(const void* __restrict__ out, const void* __restrict__ dout,
                                                            const float* __restrict__ lse, float* __restrict__ lse2,
-                                                           float* __restrict__ delta, float* __restrict__ dq_acc,
-                                                           long long o_row_stride, long long o_batch_stride, int B,
+                                                           float* __restrict__ delta, long long o_row_stride, long long o_batch_stride, int B,
                                                            int S, int S_pad, int Hq) {
   const long long total = static_cast<long long>(B) * Hq * S_pad;
   const int lane = threadIdx.x & 31;
@@ -80,37 +78,6 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(const void* __restric
       delta[wrow] = row < S ? acc : 0.f;
       lse2[wrow] = row < S ? lse[bh * S + row] * 1.4426950408889634f : INFINITY;
     }
-    float4* dq = reinterpret_cast<float4*>(dq_acc + wrow * D);
-    for (int c = lane; c < D / 4; c += 32) dq[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
-// dQ (fp32 sums) -> 16-bit rows of the caller's dQ array.
-template <int D, bool BF16>
-__global__ void __launch_bounds__(256) attn_bwd_post_kernel(const float* __restrict__ dq_acc, void* __restrict__ dq,
-                                                            long long dq_row_stride, long long dq_batch_stride, int B,
-                                                            int S, int S_pad, int Hq) {
-  // one thread converts 8 consecutive values
-  const long long per_row = D / 8;
-  const long long total = static_cast<long long>(B) * Hq * S * per_row;
-  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int c8 = static_cast<int>(idx % per_row);
-    const long long r = idx / per_row;
-    const int row = static_cast<int>(r % S);
-    const long long bh = r / S;
-    const int b = static_cast<int>(bh / Hq), h = static_cast<int>(bh % Hq);
-    const float4* src = reinterpret_cast<const float4*>(dq_acc + (bh * S_pad + row) * D + c8 * 8);
-    const float4 x = src[0], y = src[1];
-    uint4 o;
-    o.x = pack2<BF16>(x.x, x.y);
-    o.y = pack2<BF16>(x.z, x.w);
-    o.z = pack2<BF16>(y.x, y.y);
-    o.w = pack2<BF16>(y.z, y.w);
-    uint8_t* dst = reinterpret_cast<uint8_t*>(dq) +
-                   (static_cast<long long>(b) * dq_batch_stride + static_cast<long long>(row) * dq_row_stride +
-                    static_cast<long long>(h) * D + c8 * 8) * 2;
-    *reinterpret_cast<uint4*>(dst) = o;
   }
 }
 
@@ -121,27 +88,15 @@ static int grid_for(long long work, int per_block) {
 }
 
 cudaError_t attn_bwd_pre(const void* out, const void* dout, const float* lse, float* lse2, float* delta,
-                         float* dq_acc, long long o_row_stride, long long o_batch_stride, int B, int S, int S_pad,
+                         long long o_row_stride, long long o_batch_stride, int B, int S, int S_pad,
                          int Hq, int D, bool bf16, cudaStream_t st) {
   const int grid = grid_for(static_cast<long long>(B) * Hq * S_pad, 8);
 #define TKB_PRE(DD, BB) \
-  attn_bwd_pre_kernel<DD, BB><<<grid, 256, 0, st>>>(out, dout, lse, lse2, delta, dq_acc, o_row_stride, o_batch_stride, B, S, S_pad, Hq)
+  attn_bwd_pre_kernel<DD, BB><<<grid, 256, 0, st>>>(out, dout, lse, lse2, delta, o_row_stride, o_batch_stride, B, S, S_pad, Hq)
   if (D == 128) { if (bf16) TKB_PRE(128, true); else TKB_PRE(128, false); }
   else if (D == 64) { if (bf16) TKB_PRE(64, true); else TKB_PRE(64, false); }
   else return cudaErrorInvalidValue;
 #undef TKB_PRE
-  return cudaGetLastError();
-}
-
-cudaError_t attn_bwd_post(const float* dq_acc, void* dq, long long row_stride, long long batch_stride, int B, int S,
-                          int S_pad, int Hq, int D, bool bf16, cudaStream_t st) {
-  const int grid = grid_for(static_cast<long long>(B) * Hq * S * (D / 8), 256);
-#define TKB_POST(DD, BB) \
-  attn_bwd_post_kernel<DD, BB><<<grid, 256, 0, st>>>(dq_acc, dq, row_stride, batch_stride, B, S, S_pad, Hq)
-  if (D == 128) { if (bf16) TKB_POST(128, true); else TKB_POST(128, false); }
-  else if (D == 64) { if (bf16) TKB_POST(64, true); else TKB_POST(64, false); }
-  else return cudaErrorInvalidValue;
-#undef TKB_POST
   return cudaGetLastError();
 }
 

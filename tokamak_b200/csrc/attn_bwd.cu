@@ -1,53 +1,30 @@
 // attn_bwd.cu -- GQA flash-attention backward for sm_100a (tcgen05 + TMEM + TMA).
 //
 // Replaces k_gqa_flash_attn_tc_bwd<HEAD_DIM> (src/tkm_gpu.cu:440-598 of the
-// reference).  Same inputs (packed QKV, O, dO, LSE) and the same dQ math
-// (D = rowsum(O*dO), P = exp(s*scale - LSE), dS = P*(dP - D)*scale,
-// dQ = dS K), but with the true dK = dS^T Q and dV = P^T dO summed over the
-// query heads of each KV head (the reference writes dK := dQ, dV := dO at
-// src/tkm_gpu.cu:588-596).
+// reference): same inputs (packed QKV, O, dO, LSE) and math
+// (Delta = rowsum(O*dO), P = exp(s*scale - LSE), dS = P*(dP - Delta)),
+// with the true dK = scale * dS^T Q and dV = P^T dO summed over the query
+// heads of each kv head (the reference writes dK := dQ, dV := dO at
+// src/tkm_gpu.cu:588-596) and a correctly laid-out dQ = scale * dS K.
 //
-// One CTA owns a 128-key tile of one (batch, kv-head); it keeps K, V and the
-// dK, dV accumulators resident and walks every (query head of the group,
-// 128-row query tile) pair that can see those keys (causal: tiles at or
-// below the diagonal only).
-//   warps 0-3  compute warpgroup (thread = key row): P^T, dS^T
-//   warps 4-7  dQ warpgroup: drains dQ tiles from TMEM into fp32 global sums
-//   warp 8     TMA producer (K, V once; Q, dO, LSE, Delta ring)
-//   warp 9     tcgen05 MMA issuer, TMEM owner
-// Five MMAs per step, all M = 128:
-//   S^T = K Q^T, dP^T = V dO^T, dV += P^T dO (A from TMEM),
-//   dK += dS^T Q (A from TMEM), dQ = dS K (A = dS in shared memory).
+// Two kernels, no atomics, deterministic:
+//  * attn_bwd_dkdv_kernel: one CTA per 128-key tile of a (batch, kv head);
+//    K, V and the dK, dV accumulators stay resident while the CTA walks every
+//    (query head of the group, 128-row query tile) pair that sees the keys.
+//    Four MMAs per step, all M = 128 keys: S^T = K Q^T, dP^T = V dO^T,
+//    dV += P^T dO and dK += dS^T Q (P^T and dS^T read straight from TMEM).
+//  * attn_bwd_dq_kernel: one CTA per 128-row query tile of a (batch, q head),
+//    Q, dO and the dQ accumulator resident, K/V blocks streamed.  Three MMAs
+//    per block, M = 128 queries: S = Q K^T, dP = dO V^T, dQ += dS K (dS from
+//    TMEM).
+// In both kernels warps 0-7 are two compute warpgroups (one thread per TMEM
+// lane/row, each group owning half of the 128 columns), warp 8 issues TMA,
+// warp 9 issues tcgen05.mma.  The MMA order lets the next step's S/dP MMAs
+// run while the compute warps still work on the current step.
 #include "tkb_common.cuh"
 #include "tkb_internal.h"
 
 namespace tkb {
-
-template <int D>
-struct BwdCfg {
-  static constexpr int TILE = 128 * D * 2;
-  static constexpr int SLAB = 128 * 128;
-  static constexpr int NSTQ = 2;
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + TILE;
-  static constexpr int OFF_Q = OFF_V + TILE;           // NSTQ tiles
-  static constexpr int OFF_DO = OFF_Q + NSTQ * TILE;   // NSTQ tiles
-  static constexpr int OFF_DS = OFF_DO + NSTQ * TILE;  // 128 x 128 16-bit, MN-major
-  static constexpr int OFF_LSE = OFF_DS + 128 * 128 * 2;  // NSTQ x 128 floats
-  static constexpr int OFF_DEL = OFF_LSE + NSTQ * 512;    // NSTQ x 128 floats
-  static constexpr int OFF_BAR = OFF_DEL + NSTQ * 512;
-  // kv_full, q_full[NSTQ], q_empty[NSTQ], st_full, dp_full, p_ready, ds_ready, dq_full, dq_empty, kv_done, drain
-  static constexpr int NBAR = 1 + 2 * NSTQ + 8;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int USED = OFF_MISC + 16;
-  static constexpr int SLACK = (232448 - USED) < 1024 ? (232448 - USED) : 1024;
-  static constexpr int SMEM = USED + SLACK;
-  static constexpr uint32_t TM_ST = 0, TM_DP = 128;
-  static constexpr uint32_t TM_DQ = (D == 128) ? 128 : 256;
-  static constexpr uint32_t TM_DK = (D == 128) ? 256 : 320;
-  static constexpr uint32_t TM_DV = TM_DK + D;
-  static_assert(USED <= 232448, "shared memory budget");
-};
 
 TKB_DEVFN void wait_ld_dep32(uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;"
@@ -60,18 +37,36 @@ TKB_DEVFN void wait_ld_dep32(uint32_t (&r)[32]) {
                : "memory");
 }
 
+// Packed 16-bit column in TMEM of K-step kk (16 rows of the reduction dim) when
+// compute warpgroup 0 stores its half at columns [0,32) and group 1 at [64,96).
+TKB_DEVFN uint32_t half_split_col(int kk) { return kk < 4 ? kk * 8 : 64 + (kk - 4) * 8; }
+
+// ============================================================================ dK / dV
+template <int D>
+struct DkvCfg {
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int SLAB = 128 * 128;
+  static constexpr int NSTQ = 2;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + TILE;
+  static constexpr int OFF_Q = OFF_V + TILE;
+  static constexpr int OFF_DO = OFF_Q + NSTQ * TILE;
+  static constexpr int OFF_LSE = OFF_DO + NSTQ * TILE;  // NSTQ x 128 floats
+  static constexpr int OFF_DEL = OFF_LSE + NSTQ * 512;
+  static constexpr int OFF_BAR = OFF_DEL + NSTQ * 512;
+  // kv_full, q_full[NSTQ], q_empty[NSTQ], st_full, dp_full, p_ready, ds_ready, kv_done, drain
+  static constexpr int NBAR = 1 + 2 * NSTQ + 6;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;
+  static constexpr uint32_t TM_ST = 0, TM_DP = 128, TM_DK = 256, TM_DV = 256 + D;
+};
+
 template <int D, bool BF16>
-__global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_constant__ BwdParams p) {
-  using C = BwdCfg<D>;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t raw_s = smem_u32(smem_raw);
-  const uint32_t pad = (1024u - (raw_s & 1023u)) & 1023u;
-  if (pad > static_cast<uint32_t>(C::SLACK)) {
-    if (threadIdx.x == 0) atomicOr(&g_device_error, ERR_BAD_LAUNCH);
-    return;
-  }
-  uint8_t* smem = smem_raw + pad;
-  const uint32_t sbase = raw_s + pad;
+__global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_constant__ BwdParams p) {
+  using C = DkvCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
@@ -80,18 +75,14 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
   uint64_t* dp_full = st_full + 1;
   uint64_t* p_ready = dp_full + 1;
   uint64_t* ds_ready = p_ready + 1;
-  uint64_t* dq_full = ds_ready + 1;
-  uint64_t* dq_empty = dq_full + 1;
-  uint64_t* kv_done = dq_empty + 1;
+  uint64_t* kv_done = ds_ready + 1;
   uint64_t* mma_drain = kv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
-  const float* s_lse = reinterpret_cast<const float*>(smem + C::OFF_LSE);
-  const float* s_del = reinterpret_cast<const float*>(smem + C::OFF_DEL);
 
   const int warp = warp_id(), lane = lane_id();
   const int BG = p.B * p.Hkv;
-  const int jt = static_cast<int>(blockIdx.x / BG);  // kv tile; tile 0 has the most work
+  const int jt = static_cast<int>(blockIdx.x / BG);  // key tile; tile 0 sees the most queries
   const int bg = blockIdx.x % BG;
   const int b = bg / p.Hkv, g = bg % p.Hkv;
   const int G = p.Hq / p.Hkv;
@@ -108,10 +99,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
     }
     mbar_init(st_full, 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_ready, 128);
-    mbar_init(ds_ready, 128);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
+    mbar_init(p_ready, 256);
+    mbar_init(ds_ready, 256);
     mbar_init(kv_done, 1);
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
@@ -127,7 +116,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&p.tmQ);
       prefetch_tmap(&p.tmK);
@@ -167,63 +156,54 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
       }
     }
   } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+    // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idS = idesc_f16kind(128, 128, BF16, false, false);  // S^T, dP^T
       constexpr uint32_t idKV = idesc_f16kind(128, D, BF16, false, true);    // dV, dK (A in TMEM)
-      constexpr uint32_t idQ = idesc_f16kind(128, D, BF16, true, true);      // dQ (A = dS, MN-major)
-      const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V, sDS = sbase + C::OFF_DS;
-      bool ok = mbar_wait(kv_full, 0, abort_flag);
-      for (int it = 0; ok && it < n_steps; ++it) {
-        const int s = it % C::NSTQ;
-        const uint32_t sQ = sbase + C::OFF_Q + s * C::TILE, sO = sbase + C::OFF_DO + s * C::TILE;
-        if (!(ok = mbar_wait(&q_full[s], (it / C::NSTQ) & 1, abort_flag))) break;
+      const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      auto sQ = [&](int s) { return sbase + C::OFF_Q + s * C::TILE; };
+      auto sO = [&](int s) { return sbase + C::OFF_DO + s * C::TILE; };
+      auto issue_nt = [&](uint32_t d, uint32_t a, uint32_t bm) {  // D(128x128) = A(128xD) B(128xD)^T
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::SLAB + (kk & 3) * 32;
+          umma_ss(d, sdesc_sw128(a + off, 16, 1024), sdesc_sw128(bm + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_acc = [&](uint32_t d, uint32_t a_tm, uint32_t bm, bool acc) {  // D += A(tmem) B(smem, MN-major)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ts(d, a_tm + half_split_col(kk), sdesc_sw128(bm + kk * 2048, C::SLAB, 1024), idKV,
+                  (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(&q_full[0], 0, abort_flag);
+      if (ok) {
         tc_fence_after();
-        // S^T = K Q^T
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::SLAB + (kk & 3) * 32;
-          umma_ss(tmem + C::TM_ST, sdesc_sw128(sK + off, 16, 1024), sdesc_sw128(sQ + off, 16, 1024), idS,
-                  kk > 0 ? 1u : 0u);
-        }
+        issue_nt(tmem + C::TM_ST, sK, sQ(0));
         umma_commit(st_full);
-        // dP^T = V dO^T  (for D = 128 the dP region also holds the previous dQ tile)
-        if (C::TM_DQ == C::TM_DP && it > 0) {
-          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, abort_flag))) break;
-          tc_fence_after();
-        }
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::SLAB + (kk & 3) * 32;
-          umma_ss(tmem + C::TM_DP, sdesc_sw128(sV + off, 16, 1024), sdesc_sw128(sO + off, 16, 1024), idS,
-                  kk > 0 ? 1u : 0u);
-        }
+        issue_nt(tmem + C::TM_DP, sV, sO(0));
         umma_commit(dp_full);
-        // dV += P^T dO
+      }
+      for (int it = 0; ok && it < n_steps; ++it) {
+        const int s = it % C::NSTQ, s1 = (it + 1) % C::NSTQ;
+        const bool more = it + 1 < n_steps;
         if (!(ok = mbar_wait(p_ready, it & 1, abort_flag))) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + C::TM_DV, tmem + C::TM_ST + kk * 8, sdesc_sw128(sO + kk * 2048, C::SLAB, 1024), idKV,
-                  (it > 0 || kk > 0) ? 1u : 0u);
-        // dK += dS^T Q
+        issue_acc(tmem + C::TM_DV, tmem + C::TM_ST, sO(s), it > 0);           // dV += P^T dO
+        if (more) {
+          if (!(ok = mbar_wait(&q_full[s1], ((it + 1) / C::NSTQ) & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_nt(tmem + C::TM_ST, sK, sQ(s1));                              // S^T for the next step
+          umma_commit(st_full);
+        }
         if (!(ok = mbar_wait(ds_ready, it & 1, abort_flag))) break;
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + C::TM_DK, tmem + C::TM_DP + kk * 8, sdesc_sw128(sQ + kk * 2048, C::SLAB, 1024), idKV,
-                  (it > 0 || kk > 0) ? 1u : 0u);
-        // dQ = dS K  (M = queries, K = keys)
-        if (C::TM_DQ != C::TM_DP && it > 0) {
-          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, abort_flag))) break;
-          tc_fence_after();
-        }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem + C::TM_DQ, sdesc_sw128(sDS + kk * 2048, C::SLAB, 1024),
-                  sdesc_sw128(sK + kk * 2048, C::SLAB, 1024), idQ, kk > 0 ? 1u : 0u);
-        umma_commit(dq_full);
+        issue_acc(tmem + C::TM_DK, tmem + C::TM_DP, sQ(s), it > 0);           // dK += dS^T Q
         umma_commit(&q_empty[s]);
+        if (more) {
+          issue_nt(tmem + C::TM_DP, sV, sO(s1));                              // dP^T for the next step
+          umma_commit(dp_full);
+        }
       }
       if (ok) umma_commit(kv_done);
       else {
@@ -232,99 +212,103 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
         mbar_wait(mma_drain, 0, &never);
       }
     }
-  } else if (warp < 4) {
-    // ------------------------------------------------------------ compute warpgroup
-    const int kr = threadIdx.x;  // key row within the tile
+  } else {
+    // ---------------------------------------------------------------- compute warpgroups
+    const int w = warp >> 2;              // which half of the 128 query columns
+    const int kr = threadIdx.x & 127;     // key row = TMEM lane
     const int key = jt * 128 + kr;
     const bool key_ok = key < p.S;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tST = tmem + lane_off + C::TM_ST, tDP = tmem + lane_off + C::TM_DP;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t cb = static_cast<uint32_t>(w * 64);
+    const uint32_t tST = tmem + lane_off + C::TM_ST + cb, tDP = tmem + lane_off + C::TM_DP + cb;
     const float sl2 = p.scale_log2;
-    uint8_t* ds_row = smem + C::OFF_DS + kr * 128;
-    const int sw = kr & 7;
     bool ok = true;
     for (int it = 0; it < n_steps; ++it) {
       const int s = it % C::NSTQ;
       const int i = i0 + it % n_i;
-      const float* lse = s_lse + s * 128;
-      const float* del = s_del + s * 128;
-      // keys above the diagonal of a diagonal tile see nothing
-      const int qmin = (p.causal && i == jt) ? kr : 0;
-      // LSE / Delta of this stage were written by the bulk copy: observe its barrier directly.
+      const float4* lse4 = reinterpret_cast<const float4*>(smem + C::OFF_LSE + s * 512) + w * 16;
+      const float4* del4 = reinterpret_cast<const float4*>(smem + C::OFF_DEL + s * 512) + w * 16;
+      // keys above the diagonal of a diagonal tile see no query of this half below qmin
+      const int qmin = (p.causal && i == jt) ? kr - w * 64 : -1;
       if (!(ok = mbar_wait(&q_full[s], (it / C::NSTQ) & 1, abort_flag))) break;
       if (!(ok = mbar_wait(st_full, it & 1, abort_flag))) break;
       tc_fence_after();
-      uint32_t pk[64];
+      uint32_t pk[32];
+      {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tST, v0);
+        tmem_ld32(tST + 32, v1);
+        wait_ld_dep32(v0);
+        wait_ld_dep32(v1);
+        // masked keys (sequence tail) and the diagonal tile need the per-element test
+        const bool need_mask = !key_ok || qmin > 0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tST + c * 32, v);
-        wait_ld_dep32(v);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int q0 = c * 32 + 2 * e;
-          float a = ex2(fmaf(__uint_as_float(v[2 * e]), sl2, -lse[q0]));
-          float d = ex2(fmaf(__uint_as_float(v[2 * e + 1]), sl2, -lse[q0 + 1]));
-          if (!key_ok || q0 < qmin) a = 0.f;
-          if (!key_ok || q0 + 1 < qmin) d = 0.f;
-          pk[c * 16 + e] = pack2<BF16>(a, d);
+        for (int e4 = 0; e4 < 16; ++e4) {
+          const float4 l = lse4[e4];
+          const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
+          const int q0 = e4 * 4;
+          float a0 = ex2(fmaf(__uint_as_float(src[0]), sl2, -l.x));
+          float a1 = ex2(fmaf(__uint_as_float(src[1]), sl2, -l.y));
+          float a2 = ex2(fmaf(__uint_as_float(src[2]), sl2, -l.z));
+          float a3 = ex2(fmaf(__uint_as_float(src[3]), sl2, -l.w));
+          if (need_mask) {
+            if (!key_ok || q0 < qmin) a0 = 0.f;
+            if (!key_ok || q0 + 1 < qmin) a1 = 0.f;
+            if (!key_ok || q0 + 2 < qmin) a2 = 0.f;
+            if (!key_ok || q0 + 3 < qmin) a3 = 0.f;
+          }
+          pk[e4 * 2] = pack2<BF16>(a0, a1);
+          pk[e4 * 2 + 1] = pack2<BF16>(a2, a3);
         }
       }
-      tmem_st32(tST, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(tST + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      tmem_st32(tST, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_ready);
 
       if (!(ok = mbar_wait(dp_full, it & 1, abort_flag))) break;
       tc_fence_after();
-      uint32_t ds[64];
+      uint32_t ds[32];
+      {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tDP, v0);
+        tmem_ld32(tDP + 32, v1);
+        wait_ld_dep32(v0);
+        wait_ld_dep32(v1);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tDP + c * 32, v);
-        wait_ld_dep32(v);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int q0 = c * 32 + 2 * e;
-          const float2 pp = unpack2<BF16>(pk[c * 16 + e]);
-          const float a = pp.x * (__uint_as_float(v[2 * e]) - del[q0]);
-          const float d = pp.y * (__uint_as_float(v[2 * e + 1]) - del[q0 + 1]);
-          ds[c * 16 + e] = pack2<BF16>(a, d);
+        for (int e4 = 0; e4 < 16; ++e4) {
+          const float4 dl = del4[e4];
+          const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
+          const float2 p01 = unpack2<BF16>(pk[e4 * 2]), p23 = unpack2<BF16>(pk[e4 * 2 + 1]);
+          ds[e4 * 2] =
+              pack2<BF16>(p01.x * (__uint_as_float(src[0]) - dl.x), p01.y * (__uint_as_float(src[1]) - dl.y));
+          ds[e4 * 2 + 1] =
+              pack2<BF16>(p23.x * (__uint_as_float(src[2]) - dl.z), p23.y * (__uint_as_float(src[3]) - dl.w));
         }
       }
-      tmem_st32(tDP, *reinterpret_cast<uint32_t(*)[32]>(&ds[0]));
-      tmem_st32(tDP + 32, *reinterpret_cast<uint32_t(*)[32]>(&ds[32]));
-      // dS row -> shared memory, [query slab][key][64 queries] with 128-byte swizzle
-#pragma unroll
-      for (int qh = 0; qh < 2; ++qh)
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int w0 = qh * 32 + ch * 4;
-          *reinterpret_cast<uint4*>(ds_row + qh * C::SLAB + ((ch ^ sw) << 4)) =
-              make_uint4(ds[w0], ds[w0 + 1], ds[w0 + 2], ds[w0 + 3]);
-        }
-      fence_proxy_async_smem();
+      tmem_st32(tDP, ds);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(ds_ready);
     }
-    // dK epilogue
+    // epilogue: warpgroup 0 stores dK (scaled), warpgroup 1 stores dV
     if (ok && mbar_wait(kv_done, 0, abort_flag)) {
       tc_fence_after();
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.dk) +
+      const float mul = w == 0 ? p.scale : 1.0f;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(w == 0 ? p.dk : p.dv) +
                      2 * (static_cast<long long>(b) * p.dkv_batch_stride +
                           static_cast<long long>(key) * p.dkv_row_stride + static_cast<long long>(g) * D);
+      const uint32_t src_col = w == 0 ? C::TM_DK : C::TM_DV;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + C::TM_DK + c * 32, v);
+        tmem_ld32(tmem + lane_off + src_col + c * 32, v);
         wait_ld_dep32(v);
         uint4 o[4];
         uint32_t* ow = reinterpret_cast<uint32_t*>(o);
 #pragma unroll
         for (int e = 0; e < 16; ++e)
-          ow[e] = pack2<BF16>(__uint_as_float(v[2 * e]) * p.scale, __uint_as_float(v[2 * e + 1]) * p.scale);
+          ow[e] = pack2<BF16>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
         if (key_ok) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 64);
 #pragma unroll
@@ -332,47 +316,250 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
         }
       }
     }
-  } else {
-    // ------------------------------------------------------------ dQ warpgroup
-    const int qr = threadIdx.x - 128;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tDQ = tmem + lane_off + C::TM_DQ;
-    bool ok = true;
-    for (int it = 0; it < n_steps; ++it) {
-      const int hq = g * G + it / n_i, i = i0 + it % n_i;
-      if (!(ok = mbar_wait(dq_full, it & 1, abort_flag))) break;
-      tc_fence_after();
-      uint32_t v[D];
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) tmem_ld32(tDQ + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) wait_ld_dep32(*reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
-      tc_fence_before();
-      mbar_arrive(dq_empty);
-      float* dst = p.dq_acc + ((static_cast<long long>(b) * p.Hq + hq) * p.S_pad + i * 128 + qr) * D;
-      const float sc = p.scale;
-#pragma unroll
-      for (int c = 0; c < D; c += 4)
-        red_add_v4(dst + c, __uint_as_float(v[c]) * sc, __uint_as_float(v[c + 1]) * sc,
-                   __uint_as_float(v[c + 2]) * sc, __uint_as_float(v[c + 3]) * sc);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================ dQ
+template <int D>
+struct DqCfg {
+  static constexpr int TILE = 128 * D * 2;
+  static constexpr int SLAB = 128 * 128;
+  static constexpr int NST = (D == 64) ? 4 : 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_DO = OFF_Q + TILE;
+  static constexpr int OFF_K = OFF_DO + TILE;
+  static constexpr int OFF_V = OFF_K + NST * TILE;
+  static constexpr int OFF_BAR = OFF_V + NST * TILE;
+  // q_full, kv_full[NST], kv_empty[NST], s_full[2], dp_full, ds_ready, dq_done, drain
+  static constexpr int NBAR = 1 + 2 * NST + 6;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;
+  static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_DP = 256, TM_DQ = 384;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+  using C = DqCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = kv_full + C::NST;
+  uint64_t* s_full = kv_empty + C::NST;
+  uint64_t* dp_full = s_full + 2;
+  uint64_t* ds_ready = dp_full + 1;
+  uint64_t* dq_done = ds_ready + 1;
+  uint64_t* mma_drain = dq_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int BH = p.B * p.Hq;
+  const int nq = p.S_pad >> 7;
+  const int qt = nq - 1 - static_cast<int>(blockIdx.x / BH);  // longest (causal) first
+  const int bh = blockIdx.x % BH;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int g = h / (p.Hq / p.Hkv);
+  const int nkv = (p.S + 127) >> 7;
+  const int nb = p.causal ? min(qt + 1, nkv) : nkv;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
     }
-    // dV epilogue
-    if (ok && mbar_wait(kv_done, 0, abort_flag)) {
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
+    mbar_init(dp_full, 1);
+    mbar_init(ds_ready, 256);
+    mbar_init(dq_done, 1);
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&p.tmQ);
+      prefetch_tmap(&p.tmK);
+      prefetch_tmap(&p.tmV);
+      prefetch_tmap(&p.tmdO);
+      const uint64_t pol_q = policy_evict_first(), pol_kv = policy_evict_last();
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE);
+#pragma unroll
+      for (int hh = 0; hh < D / 64; ++hh) {
+        tma_load_3d(smem + C::OFF_Q + hh * C::SLAB, &p.tmQ, q_full, h * D + hh * 64, qt * 128, b, pol_q);
+        tma_load_3d(smem + C::OFF_DO + hh * C::SLAB, &p.tmdO, q_full, h * D + hh * 64, qt * 128, b, pol_q);
+      }
+      int issued = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j % C::NST;
+        if (!mbar_wait(&kv_empty[s], ((j / C::NST) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::TILE);
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh) {
+          tma_load_3d(smem + C::OFF_K + s * C::TILE + hh * C::SLAB, &p.tmK, &kv_full[s], g * D + hh * 64, j * 128,
+                      b, pol_kv);
+          tma_load_3d(smem + C::OFF_V + s * C::TILE + hh * C::SLAB, &p.tmV, &kv_full[s], g * D + hh * 64, j * 128,
+                      b, pol_kv);
+        }
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        mbar_wait(q_full, 0, &never);
+        for (int j = max(0, issued - C::NST); j < issued; ++j)
+          mbar_wait(&kv_full[j % C::NST], (j / C::NST) & 1, &never);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_f16kind(128, 128, BF16, false, false);  // S, dP
+      constexpr uint32_t idQ = idesc_f16kind(128, D, BF16, false, true);     // dQ (A = dS in TMEM)
+      const uint32_t sQ = sbase + C::OFF_Q, sO = sbase + C::OFF_DO;
+      auto sK = [&](int s) { return sbase + C::OFF_K + s * C::TILE; };
+      auto sV = [&](int s) { return sbase + C::OFF_V + s * C::TILE; };
+      auto tS = [&](int j) { return tmem + ((j & 1) ? C::TM_S1 : C::TM_S0); };
+      auto issue_nt = [&](uint32_t d, uint32_t a, uint32_t bm) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::SLAB + (kk & 3) * 32;
+          umma_ss(d, sdesc_sw128(a + off, 16, 1024), sdesc_sw128(bm + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&kv_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_nt(tS(0), sQ, sK(0));
+        umma_commit(&s_full[0]);
+        issue_nt(tmem + C::TM_DP, sO, sV(0));
+        umma_commit(dp_full);
+      }
+      for (int j = 0; ok && j < nb; ++j) {
+        const int s = j % C::NST, s1 = (j + 1) % C::NST;
+        const bool more = j + 1 < nb;
+        if (more) {
+          if (!(ok = mbar_wait(&kv_full[s1], ((j + 1) / C::NST) & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_nt(tS(j + 1), sQ, sK(s1));                                    // S for the next block
+          umma_commit(&s_full[(j + 1) & 1]);
+        }
+        if (!(ok = mbar_wait(ds_ready, j & 1, abort_flag))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)                                         // dQ += dS K
+          umma_ts(tmem + C::TM_DQ, tS(j) + half_split_col(kk), sdesc_sw128(sK(s) + kk * 2048, C::SLAB, 1024), idQ,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&kv_empty[s]);
+        if (more) {
+          issue_nt(tmem + C::TM_DP, sO, sV(s1));                              // dP for the next block
+          umma_commit(dp_full);
+        }
+      }
+      if (ok) umma_commit(dq_done);
+      else {
+        volatile int never = 0;
+        umma_commit(mma_drain);
+        mbar_wait(mma_drain, 0, &never);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- compute warpgroups
+    const int w = warp >> 2;             // which half of the 128 keys of a block
+    const int r = threadIdx.x & 127;     // query row = TMEM lane
+    const int qrow = qt * 128 + r;
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t cb = static_cast<uint32_t>(w * 64);
+    const long long rowi = static_cast<long long>(bh) * p.S_pad + qrow;
+    const float lse2 = p.lse2[rowi], dlt = p.delta[rowi];
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    for (int j = 0; j < nb; ++j) {
+      const uint32_t tSj = tmem + lane_off + ((j & 1) ? C::TM_S1 : C::TM_S0) + cb;
+      const int kbase = j * 128 + w * 64;
+      // keys >= lim are masked (sequence end, causal diagonal)
+      const int lim = min(p.S - kbase, p.causal ? qrow - kbase + 1 : 64);
+      if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag))) break;
       tc_fence_after();
-      const int key = jt * 128 + qr;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.dv) +
+      float pv[64];
+      {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tSj, v0);
+        tmem_ld32(tSj + 32, v1);
+        wait_ld_dep32(v0);
+        wait_ld_dep32(v1);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          pv[c] = ex2(fmaf(__uint_as_float(v0[c]), sl2, -lse2));
+          pv[c + 1] = ex2(fmaf(__uint_as_float(v0[c + 1]), sl2, -lse2));
+          pv[32 + c] = ex2(fmaf(__uint_as_float(v1[c]), sl2, -lse2));
+          pv[32 + c + 1] = ex2(fmaf(__uint_as_float(v1[c + 1]), sl2, -lse2));
+        }
+        if (lim < 64) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (c >= lim) pv[c] = 0.f;
+        }
+      }
+      if (!(ok = mbar_wait(dp_full, j & 1, abort_flag))) break;
+      tc_fence_after();
+      uint32_t ds[32];
+      {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(tmem + lane_off + C::TM_DP + cb, v0);
+        tmem_ld32(tmem + lane_off + C::TM_DP + cb + 32, v1);
+        wait_ld_dep32(v0);
+        wait_ld_dep32(v1);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          ds[e] = pack2<BF16>(pv[2 * e] * (__uint_as_float(v0[2 * e]) - dlt),
+                                   pv[2 * e + 1] * (__uint_as_float(v0[2 * e + 1]) - dlt));
+          ds[16 + e] = pack2<BF16>(pv[32 + 2 * e] * (__uint_as_float(v1[2 * e]) - dlt),
+                                        pv[32 + 2 * e + 1] * (__uint_as_float(v1[2 * e + 1]) - dlt));
+        }
+      }
+      tmem_st32(tSj, ds);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+    }
+    // epilogue: each warpgroup stores half of the D columns of dQ (scaled)
+    if (ok && mbar_wait(dq_done, 0, abort_flag)) {
+      tc_fence_after();
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.dq) +
                      2 * (static_cast<long long>(b) * p.dkv_batch_stride +
-                          static_cast<long long>(key) * p.dkv_row_stride + static_cast<long long>(g) * D);
+                          static_cast<long long>(qrow) * p.dkv_row_stride + static_cast<long long>(h) * D);
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = w * (D / 64); c < (w + 1) * (D / 64); ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + C::TM_DV + c * 32, v);
+        tmem_ld32(tmem + lane_off + C::TM_DQ + c * 32, v);
         wait_ld_dep32(v);
         uint4 o[4];
         uint32_t* ow = reinterpret_cast<uint32_t*>(o);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) ow[e] = pack2<BF16>(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
-        if (key < p.S) {
+        for (int e = 0; e < 16; ++e)
+          ow[e] = pack2<BF16>(__uint_as_float(v[2 * e]) * p.scale, __uint_as_float(v[2 * e + 1]) * p.scale);
+        if (qrow < p.S) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 64);
 #pragma unroll
           for (int e = 0; e < 4; ++e) d4[e] = o[e];
@@ -391,13 +578,22 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_tc_kernel(const __grid_consta
 
 template <int D, bool BF16>
 static cudaError_t launch_bwd(const BwdParams& p, cudaStream_t stream) {
-  using C = BwdCfg<D>;
-  auto kern = attn_bwd_tc_kernel<D, BF16>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-  if (e != cudaSuccess) return e;
-  const unsigned grid = static_cast<unsigned>(p.B * p.Hkv * (p.S_pad / 128));
-  kern<<<grid, 320, C::SMEM, stream>>>(p);
-  return cudaGetLastError();
+  {
+    using C = DkvCfg<D>;
+    auto kern = attn_bwd_dkdv_kernel<D, BF16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    kern<<<static_cast<unsigned>(p.B * p.Hkv * (p.S_pad / 128)), 320, C::SMEM, stream>>>(p);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  {
+    using C = DqCfg<D>;
+    auto kern = attn_bwd_dq_kernel<D, BF16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    kern<<<static_cast<unsigned>(p.B * p.Hq * (p.S_pad / 128)), 320, C::SMEM, stream>>>(p);
+    return cudaGetLastError();
+  }
 }
 
 cudaError_t attn_bwd_tc(const BwdParams& p, int D, bool bf16, cudaStream_t stream) {

@@ -13,9 +13,8 @@ namespace tkb {
 cudaError_t attn_f32_fwd(const float*, float*, float*, int, int, int, int, int, float, int, cudaStream_t);
 cudaError_t attn_f32_bwd(const float*, const float*, const float*, const float*, float*, int, int, int, int, int,
                          float, int, cudaStream_t);
-cudaError_t attn_bwd_pre(const void*, const void*, const float*, float*, float*, float*, long long, long long, int,
-                         int, int, int, int, bool, cudaStream_t);
-cudaError_t attn_bwd_post(const float*, void*, long long, long long, int, int, int, int, int, bool, cudaStream_t);
+cudaError_t attn_bwd_pre(const void*, const void*, const float*, float*, float*, long long, long long, int, int, int,
+                         int, int, bool, cudaStream_t);
 }  // namespace tkb
 
 namespace {
@@ -114,7 +113,7 @@ size_t tkb_gqa_attn_bwd_workspace(int B, int S, int Hq, int D, int dtype) {
   if (dtype == TKB_F32 || B <= 0 || S <= 0 || Hq <= 0 || D <= 0) return 0;
   const size_t spad = static_cast<size_t>((S + 127) / 128) * 128;
   const size_t rows = static_cast<size_t>(B) * Hq * spad;
-  return round256(rows * D * 4) + 2 * round256(rows * 4);
+  return 2 * round256(rows * 4);
 }
 
 int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, void* dqkv,
@@ -138,12 +137,11 @@ int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const f
   const int S_pad = (S + 127) / 128 * 128;
   const size_t rows = static_cast<size_t>(B) * Hq * S_pad;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  float* dq_acc = reinterpret_cast<float*>(ws);
-  float* lse2 = reinterpret_cast<float*>(ws + round256(rows * D * 4));
-  float* delta = reinterpret_cast<float*>(ws + round256(rows * D * 4) + round256(rows * 4));
+  float* lse2 = reinterpret_cast<float*>(ws);
+  float* delta = reinterpret_cast<float*>(ws + round256(rows * 4));
   const long long ld = static_cast<long long>(Hq + 2 * Hkv) * D, ldo = static_cast<long long>(Hq) * D;
 
-  cudaError_t e = attn_bwd_pre(out, dout, lse, lse2, delta, dq_acc, ldo, ldo * S, B, S, S_pad, Hq, D, bf16, st);
+  cudaError_t e = attn_bwd_pre(out, dout, lse, lse2, delta, ldo, ldo * S, B, S, S_pad, Hq, D, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "tkb_gqa_attn_bwd: preprocess", 0);
 
   BwdParams p;
@@ -160,8 +158,8 @@ int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const f
   if (e != cudaSuccess) return cuda_status(e, "tkb_gqa_attn_bwd: tensor map", 0);
   p.lse2 = lse2;
   p.delta = delta;
-  p.dq_acc = dq_acc;
   uint16_t* dbase = static_cast<uint16_t*>(dqkv);
+  p.dq = dbase;
   p.dk = dbase + static_cast<long long>(Hq) * D;
   p.dv = dbase + static_cast<long long>(Hq + Hkv) * D;
   p.dkv_row_stride = ld;
@@ -175,9 +173,7 @@ int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const f
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   e = attn_bwd_tc(p, D, bf16, st);
-  if (e != cudaSuccess) return cuda_status(e, "tkb_gqa_attn_bwd: main kernel", 1);
-  e = attn_bwd_post(dq_acc, dqkv, ld, ld * S, B, S, S_pad, Hq, D, bf16, st);
-  return cuda_status(e, "tkb_gqa_attn_bwd: postprocess", 3);
+  return cuda_status(e, "tkb_gqa_attn_bwd: dK/dV and dQ kernels", 3);
 }
 
 }  // extern "C"

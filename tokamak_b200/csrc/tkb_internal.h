@@ -27,10 +27,10 @@ struct alignas(64) BwdParams {
   CUtensorMap tmQ, tmK, tmV, tmdO;
   const float* lse2;          // [B*Hq][S_pad]  LSE * log2(e), +inf on padded rows
   const float* delta;         // [B*Hq][S_pad]  rowsum(O * dO), 0 on padded rows
-  float* dq_acc;              // [B*Hq][S_pad][D] fp32, zeroed before the kernel
-  void* dk;                   // row-major, dk_row_stride elements per row, head g at g*D
+  void* dq;                   // row-major, dkv_row_stride elements per row, head h at h*D
+  void* dk;                   // row-major, dkv_row_stride elements per row, head g at g*D
   void* dv;
-  long long dkv_row_stride;   // elements
+  long long dkv_row_stride;   // elements (dQ, dK, dV share the packed layout)
   long long dkv_batch_stride; // elements
   int B, S, S_pad, Hq, Hkv;
   int causal;
