@@ -29,8 +29,8 @@ struct FwdCfg {
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
   static constexpr int OFF_V = OFF_K + NST * TILE;
   static constexpr int OFF_BAR = OFF_V + NST * TILE;
-  // q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST], s_full[2], p_ready[2], o_done[2], drain
-  static constexpr int NBAR = 1 + 4 * NST + 7;
+  // q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST], s_full[2], p_ready[2][2], o_done[2], drain
+  static constexpr int NBAR = 1 + 4 * NST + 9;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
@@ -60,8 +60,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
   uint64_t* v_full = k_empty + C::NST;
   uint64_t* v_empty = v_full + C::NST;
   uint64_t* s_full = v_empty + C::NST;
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* o_done = p_ready + 2;
+  uint64_t* p_ready = s_full + 2;  // [w][half]: P of keys 0-63 / 64-127 of the block is in TMEM
+  uint64_t* o_done = p_ready + 4;
   uint64_t* mma_drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
@@ -91,7 +91,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(&s_full[w], 1);
-      mbar_init(&p_ready[w], 128);
+      mbar_init(&p_ready[2 * w], 128);
+      mbar_init(&p_ready[2 * w + 1], 128);
       mbar_init(&o_done[w], 1);
     }
     mbar_init(mma_drain, 1);
@@ -166,13 +167,16 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
                   sdesc_sw128(ka + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
         }
       };
-      auto issue_PV = [&](int w, int s, bool acc) {
+      // O += P V over the keys of one half of the block (k-steps 4*half .. 4*half+3)
+      auto issue_PV = [&](int w, int s, int half, bool acc) {
         const uint32_t va = sV + s * C::TILE;
         const uint32_t tP = tmem + (w ? C::TM_S1 : C::TM_S0);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = half * 4 + k4;
           umma_ts(tmem + (w ? C::TM_O1 : C::TM_O0), tP + kk * 8, sdesc_sw128(va + kk * 2048, C::SLAB, 1024), idO,
                   (acc || kk > 0) ? 1u : 0u);
+        }
       };
       bool ok = mbar_wait(q_full, 0, abort_flag) && mbar_wait(&k_full[0], 0, abort_flag);
       if (ok) {
@@ -190,9 +194,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         bool k_next = false;
         for (int w = 0; w < 2 && ok; ++w) {
           if (j >= nb[w]) continue;
-          if (!(ok = mbar_wait(&p_ready[w], j & 1, abort_flag))) break;
+          if (!(ok = mbar_wait(&p_ready[2 * w], j & 1, abort_flag))) break;
           tc_fence_after();
-          issue_PV(w, s, j > 0);
+          issue_PV(w, s, 0, j > 0);
+          if (!(ok = mbar_wait(&p_ready[2 * w + 1], j & 1, abort_flag))) break;
+          tc_fence_after();
+          issue_PV(w, s, 1, true);
           if (j == nb[w] - 1) umma_commit(&o_done[w]);
           if (j + 1 < nb[w]) {
             if (!k_next) {
@@ -282,6 +289,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       const float nm = -m_used;
       uint32_t pk0[32], pk1[32];
       float ls0 = 0.f, ls1 = 0.f;
+      // P for keys 0-63 goes to TMEM first so that the P*V MMA can start on
+      // that half while the exponentials of keys 64-127 are computed.
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float a = ex2(fmaf(sv[2 * i], sl2, nm));
@@ -290,6 +299,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         ls1 += c;
         pk0[i] = pack2<BF16>(a, c);
       }
+      tmem_st32(tS + 0, pk0);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_ready[2 * w]);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float a = ex2(fmaf(sv[64 + 2 * i], sl2, nm));
@@ -299,11 +312,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         pk1[i] = pack2<BF16>(a, c);
       }
       l += ls0 + ls1;
-      tmem_st32(tS + 0, pk0);
       tmem_st32(tS + 32, pk1);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_ready[w]);
+      mbar_arrive(&p_ready[2 * w + 1]);
     }
     if (ok && nb[w] > 0 && mbar_wait(&o_done[w], 0, abort_flag)) {
       tc_fence_after();
