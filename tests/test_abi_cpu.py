@@ -63,3 +63,34 @@ def test_workspace_sizes():
     assert L.tkb_gqa_attn_bwd_workspace(8, 4096, 16, 128, 0) == 0
     assert L.tkb_add_rmsnorm_bwd_workspace(16384, 4096) > 0
     assert L.tkb_softmax_loss_workspace(8192) >= 8192 * 4
+
+
+def declared_tkm():
+    text = open(os.path.join(ROOT, "include", "tkm.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(tkm_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_engine_exports_every_tkm_h_function():
+    import tokamak_b200
+    L = tokamak_b200.engine()
+    names = declared_tkm()
+    assert len(names) >= 45, names
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+
+
+def test_engine_runtime_calls_fail_cleanly_without_gpu():
+    """Runtime entry points return NULL / 0 with a message instead of exiting
+    (the reference exits the process on CUDA errors)."""
+    import ctypes
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("host has a GPU")
+    from tokamak_b200 import runtime
+    L = runtime.lib()
+    assert not L.tkm_load_string_ex(b"input: 1x1x32\nt: SiLU -> SoftmaxCE", 2, 1)
+    assert runtime.last_error()
+    assert L.tkm_runtime_weight_bytes(None) == 0
+    assert L.tkm_runtime_input_elements(None) == 0
+    assert not L.tkm_load_string(None, 2)

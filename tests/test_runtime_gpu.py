@@ -1,0 +1,301 @@
+"""The Tokamak engine (libtkm.so: DSL -> fused graph -> NVRTC sm_100a plasma
+kernels + cuBLAS + libtkm_b200 kernels, step captured as a CUDA graph)
+against the float64 graph oracle (oracle/graph_oracle.py) and against
+finite differences, the way the reference's own `tkm numcheck` tests its
+GPU path (src/main.c:77-143, 253-304).
+
+Tolerances: fp32 mode 1e-4 relative L2 on loss, logits, input and parameter
+gradients and updated weights; bf16 mode loss within 1 %, logits within 2e-2
+and gradients within 5e-2 relative L2 (bf16 activations through every layer)."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def runtime_mod():
+    from tokamak_b200 import runtime
+    return runtime
+
+
+def oracle_for(dsl, batch):
+    from oracle.graph_oracle import oracle_for as make, reference_front_end
+    fe = reference_front_end()
+    if fe is None:  # the reference's host build is missing: use ours (pinned equal on CPU)
+        from oracle.tkm_abi import bind
+        from tokamak_b200 import engine
+        fe = bind(engine())
+    return make(dsl, batch, fe)
+
+
+def random_params(orc, rng, scale=0.02, gain_sd=0.1, bias_sd=0.02):
+    out = []
+    for node, kind, size in orc.tensors:
+        if kind == 0:
+            out.append(rng.normal(0.0, scale, size))
+        elif kind == 1:
+            out.append(1.0 + rng.normal(0.0, gain_sd, size))
+        else:
+            out.append(rng.normal(0.0, bias_sd, size))
+    return [np.asarray(a, np.float32) for a in out]
+
+
+def compare_step(dsl, batch, dtype, rng, tol_loss, tol_logits, tol_grad, labels_fn=None, lr=0.0, x=None):
+    rt_mod = runtime_mod()
+    orc = oracle_for(dsl, batch)
+    params = random_params(orc, rng)
+    orc.set_params([p.astype(np.float64) for p in params])
+    rt = rt_mod.Runtime.from_dsl(dsl, batch, dtype)
+    assert rt.param_count() == len(orc.tensors)
+    rt.load_weights(rt_mod.tkm1_pack(params))
+    n_in = rt.input_elements
+    if x is None:
+        x = rng.normal(0.0, 1.0, n_in).astype(np.float32)
+    from oracle.graph_oracle import LOSS_OPS
+    loss_node = [i for i in range(orc.n) if not orc.nodes[i].dead and orc.nodes[i].op in LOSS_OPS][-1]
+    rows = orc.rows(loss_node)
+    C = orc.C[orc.nodes[loss_node].in0]
+    y = labels_fn(rows, C) if labels_fn else rng.integers(0, C, rows).astype(np.int32)
+    ref = orc.run(x.astype(np.float64), y)
+    loss = rt.step(x, y, lr)
+    assert abs(loss - ref["loss"]) <= tol_loss * abs(ref["loss"]), (loss, ref["loss"])
+    logits = rt.logits(rows * C)
+    assert rel_l2(logits, ref["acts"][orc.nodes[loss_node].in0].ravel()) <= tol_logits
+    assert rel_l2(rt.input_grad(), ref["dinput"].ravel()) <= tol_grad
+    worst = 0.0
+    for t, (node, kind, size) in enumerate(orc.tensors):
+        g = rt.param_grad(t, size)
+        want = ref["grads"].get(t)
+        if want is None or np.linalg.norm(want) < 1e-12:
+            assert np.allclose(g, 0.0), (t, node, kind)
+            continue
+        e = rel_l2(g, want)
+        worst = max(worst, e)
+        assert e <= tol_grad, (t, node, kind, e)
+    return rt, orc, params, ref, worst
+
+
+def test_llama_c1_fp32_step_matches_oracle():
+    from tokamak_b200.configs import C1, dsl_for
+    rt_mod = runtime_mod()
+    rng = np.random.default_rng(7)
+    rt, orc, params, ref, worst = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_F32, rng, 1e-4, 1e-4, 1e-4)
+    # one SGD step (lr 0.05) moves every weight as the reference's SGD does
+    x = rng.normal(0.0, 1.0, rt.input_elements).astype(np.float32)
+    y = rng.integers(0, C1["vocab"], C1["batch"] * C1["seq"]).astype(np.int32)
+    ref = orc.run(x.astype(np.float64), y)
+    rt.step(x, y, 0.05)
+    new_p, _ = orc.sgd_update(ref["grads"], 0.05)
+    got = rt_mod.tkm1_unpack(rt.save_weights())
+    for t in range(len(new_p)):
+        if t in ref["grads"]:
+            assert rel_l2(got[t], new_p[t]) <= 1e-5, t
+    rt.close()
+
+
+def test_llama_c1_bf16_step_matches_oracle():
+    from tokamak_b200.configs import C1, dsl_for
+    rt_mod = runtime_mod()
+    rt, *_ = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(8), 1e-2, 2e-2, 5e-2)
+    rt.close()
+
+
+def test_llama_tied_embeddings_c1():
+    """Configuration 1 end to end: tied embedding matrix E (input rows are
+    E[token], the head FC weight is E^T), next-token labels; dE gathers the
+    input gradient by token and adds the head weight gradient."""
+    from tokamak_b200.configs import C1, dsl_for
+    rt_mod = runtime_mod()
+    rng = np.random.default_rng(11)
+    dsl = dsl_for(C1)
+    orc = oracle_for(dsl, C1["batch"])
+    params = random_params(orc, rng)
+    V, d = C1["vocab"], C1["d_model"]
+    E = rng.normal(0.0, 0.02, (V, d)).astype(np.float32)
+    head = [t for t, (node, kind, size) in enumerate(orc.tensors) if kind == 0 and size == d * V][-1]
+    params[head] = np.ascontiguousarray(E.T).ravel()
+    tokens = rng.integers(0, V, (C1["batch"], C1["seq"] + 1))
+    x = E[tokens[:, :-1]].reshape(-1)
+    y = tokens[:, 1:].reshape(-1).astype(np.int32)
+    rt = rt_mod.Runtime.from_dsl(dsl, C1["batch"], rt_mod.DTYPE_F32)
+    rt.load_weights(rt_mod.tkm1_pack(params))
+    orc.set_params([p.astype(np.float64) for p in params])
+    ref = orc.run(x.astype(np.float64), y)
+    loss = rt.step(x, y, 0.0)
+    assert abs(loss - ref["loss"]) <= 1e-4 * ref["loss"]
+
+    def dE(dinput, dW):
+        g = np.zeros((V, d))
+        np.add.at(g, tokens[:, :-1].reshape(-1), dinput.reshape(-1, d))
+        return g + dW.reshape(d, V).T
+
+    got = dE(rt.input_grad().astype(np.float64), rt.param_grad(head, d * V).astype(np.float64))
+    want = dE(ref["dinput"], ref["grads"][head])
+    assert rel_l2(got, want) <= 1e-4
+    rt.close()
+
+
+FLUID_OPS = ["SiLU", "ReLU", "ReLU2", "LeakyReLU", "ELU", "GELU", "Mish", "HardSwish", "HardSigmoid", "Tanh",
+             "Sigmoid", "SwishBeta", "Sin", "CosGate", "SoftCap", "Clamp", "Scale(0.7)", "LayerScale", "DyT",
+             "PReLU", "xATLU", "Softplus", "Snake(1.7)"]
+
+
+@pytest.mark.parametrize("op", FLUID_OPS)
+def test_fluid_op_numcheck(op):
+    """The reference's GPU calculus audit (src/main.c:253-304): a 32-wide
+    input through one operator into SoftmaxCE, batch 2, labels {3, 7};
+    analytic input gradient vs a central difference (eps 1e-3, tol 5e-3),
+    and the whole gradient vs the float64 oracle."""
+    rt_mod = runtime_mod()
+    dsl = f"input: 1x1x32\ntest: {op} -> SoftmaxCE"
+    rt = rt_mod.Runtime.from_dsl(dsl, 2, rt_mod.DTYPE_F32)
+    x = (np.sin(np.arange(64) * 0.4) * 1.5 + 0.2).astype(np.float32)
+    x[np.abs(x) < 0.1] = 0.5
+    y = np.array([3, 7], np.uint8)
+    rt.step(x, y, 0.0)
+    ana = rt.grad_sample(0, 8)
+    eps = 1e-3
+    xp = x.copy()
+    xp[8] += eps
+    rt.step(xp, y, 0.0)
+    lp = rt.eval_current_loss()
+    xm = x.copy()
+    xm[8] -= eps
+    rt.step(xm, y, 0.0)
+    lm = rt.eval_current_loss()
+    num = (lp - lm) / (2 * eps)
+    assert abs(ana - num) / max(1.0, abs(ana), abs(num)) < 5e-3, (op, ana, num)
+    # against the oracle (one label per sample, as the reference's uint8 path)
+    orc = oracle_for(dsl, 2)
+    orc.set_params([p.astype(np.float64) for p in rt_mod.tkm1_unpack(rt.save_weights())])
+    ref = orc.run(x.astype(np.float64), np.array([3, 7], np.int32))
+    rt.step(x, y, 0.0)
+    assert rel_l2(rt.input_grad(), ref["dinput"].ravel()) <= 1e-4, op
+    rt.close()
+
+
+def test_fused_twin_user_fluid_graph():
+    """The reference's fused-graph check (src/main.c:77-143): twin-FC fusion
+    with custom Softplus around it; input gradients vs central differences
+    (eps 5e-2, tol 1e-2) and vs the oracle."""
+    rt_mod = runtime_mod()
+    dsl = ("input: 1x1x8\nflow:\n  trunk: FC(8) -> Softplus -> FC(8) -> Tanh\n  gate: {\n"
+           "    branch: FC(8) -> Softplus -> Scale(0.7)\n    skip: FC(8) -> GELU\n"
+           "  } -> Mul -> Softplus -> FC(4) -> SoftmaxCE\n")
+    x = np.array([0.4, -0.2, 0.8, -0.5, 0.3, 0.7, -0.1, 0.6, 0.2, 0.5, -0.4, 0.1, 0.8, -0.3, 0.6, -0.7,
+                  -0.2, 0.3, 0.4, 0.6, -0.8, 0.2, 0.1, 0.5, 0.7, -0.5, 0.2, 0.4, 0.3, -0.1, 0.8, -0.4], np.float32)
+    y = np.array([1, 0, 3, 2], np.uint8)
+    for dtype in (rt_mod.DTYPE_F32, rt_mod.DTYPE_BF16):
+        rt = rt_mod.Runtime.from_dsl(dsl, 4, dtype)
+        loss = rt.step(x, y, 0.0)
+        assert np.isfinite(loss)
+        eps = 5e-2
+        for i in range(8):
+            xp, xm = x.copy(), x.copy()
+            xp[i] += eps
+            xm[i] -= eps
+            lp = rt.step(xp, y, 0.0)
+            lm = rt.step(xm, y, 0.0)
+            rt.step(x, y, 0.0)
+            ana = rt.grad_sample(0, i)
+            assert abs(ana - (lp - lm) / (2 * eps)) <= 1e-2, (dtype, i)
+        if dtype == rt_mod.DTYPE_F32:
+            orc = oracle_for(dsl, 4)
+            orc.set_params([p.astype(np.float64) for p in rt_mod.tkm1_unpack(rt.save_weights())])
+            ref = orc.run(x.astype(np.float64), np.array([1, 0, 3, 2], np.int32))
+            assert rel_l2(rt.input_grad(), ref["dinput"].ravel()) <= 1e-4
+        rt.close()
+
+
+@pytest.mark.parametrize("name", ["norms_and_params", "gqa_qknorm_rope"])
+def test_other_graphs_match_oracle(name):
+    rt_mod = runtime_mod()
+    dsl = {
+        "norms_and_params": """
+input: 1x4x96
+flow:
+  a: FC(128) -> LN -> PReLU -> xATLU
+  b: { p: FC(128) -> Mish -> DyT, q: Identity } -> Add -> BN -> LayerScale -> L2Norm
+  c: FC(64) -> Softmax -> FC(10) -> SoftmaxFocal(gamma=2.5)
+""",
+        "gqa_qknorm_rope": """
+input: 1x64x256
+flow:
+  blk: {
+    branch: RMSNorm -> {
+      q: FC(256) -> QKNorm -> RoPE(theta=500000, scale=8, low_freq_factor=1, high_freq_factor=4, original_context_length=16)
+      k: FC(128) -> QKNorm -> RoPE(theta=500000, scale=8, low_freq_factor=1, high_freq_factor=4, original_context_length=16)
+      v: FC(128)
+    } -> GQA(q=4, kv=2, d=64, causal=true) -> FC(256) -> SoftCap(50.0)
+    skip: Identity
+  } -> Add
+  head: RMSNorm -> FC(64) -> SoftmaxMSE
+""",
+    }[name]
+    rt, *_ = compare_step(dsl, 3, rt_mod.DTYPE_F32, np.random.default_rng(5), 1e-4, 1e-4, 1e-4)
+    rt.close()
+
+
+def test_weights_roundtrip_forward_and_eval():
+    """TKM1 save/load between a training and an inference runtime; forward
+    output equals the training runtime's logits; eval counts argmax hits."""
+    rt_mod = runtime_mod()
+    from tokamak_b200 import runtime as R
+    dsl_train = "input: 1x1x64\nflow:\n  m: FC(128) -> RMSNorm -> SiLU -> FC(10) -> SoftmaxCE\n"
+    dsl_infer = "input: 1x1x64\nflow:\n  m: FC(128) -> RMSNorm -> SiLU -> FC(10)\n"
+    rng = np.random.default_rng(3)
+    tr = rt_mod.Runtime.from_dsl(dsl_train, 16, rt_mod.DTYPE_F32)
+    x = rng.normal(0, 1, tr.input_elements).astype(np.float32)
+    y = rng.integers(0, 10, 16).astype(np.uint8)
+    for _ in range(5):
+        tr.step(x, y, 0.05)
+    blob = tr.save_weights()
+    tr.step(x, y, 0.0)  # lr 0 leaves the weights as saved
+    logits = tr.logits(16 * 10)
+    inf = R.Runtime(R.lib().tkm_load_string_ex(dsl_infer.encode(), 16, rt_mod.DTYPE_F32))
+    inf.load_weights(blob)
+    out = inf.forward(x)
+    assert rel_l2(out, logits) <= 1e-5
+    correct = tr.eval(x, y, 16)
+    assert correct == int((logits.reshape(16, 10).argmax(1) == y).sum())
+    # a partial final batch counts only the valid samples
+    assert tr.eval(x, y, 5) == int((logits.reshape(16, 10)[:5].argmax(1) == y[:5]).sum())
+    tr.close()
+    inf.close()
+
+
+def test_training_reduces_loss_and_is_deterministic():
+    rt_mod = runtime_mod()
+    from tokamak_b200.configs import C1, dsl_for
+    rng = np.random.default_rng(21)
+    dsl = dsl_for(C1)
+    x = rng.normal(0, 1, C1["batch"] * C1["seq"] * C1["d_model"]).astype(np.float32)
+    y = rng.integers(0, C1["vocab"], C1["batch"] * C1["seq"]).astype(np.int32)
+    runs = []
+    for _ in range(2):
+        rt = rt_mod.Runtime.from_dsl(dsl, C1["batch"], rt_mod.DTYPE_BF16)
+        losses = [rt.step(x, y, 0.05) for _ in range(12)]
+        runs.append((losses, rt.save_weights()))
+        rt.close()
+    assert runs[0][0][-1] < runs[0][0][0] - 0.5, runs[0][0]
+    assert runs[0][0] == runs[1][0]
+    assert runs[0][1] == runs[1][1]
+
+
+def test_rejects_bad_labels_and_foreign_source():
+    rt_mod = runtime_mod()
+    rt = rt_mod.Runtime.from_dsl("input: 1x1x32\nt: SiLU -> SoftmaxCE", 2, rt_mod.DTYPE_F32)
+    with pytest.raises(Exception):
+        rt.step(np.zeros(64, np.float32), np.array([3, 40], np.int32), 0.0)
+    rt.close()
+    R = rt_mod
+    import ctypes
+    from oracle.tkm_abi import Graph, bind, compile_graph
+    from tokamak_b200 import engine
+    lib = bind(engine())
+    g = compile_graph(lib, "input: 1x1x32\nt: SiLU -> SoftmaxCE", 2)
+    h = R.lib().tkm_runtime_ignite(ctypes.cast(ctypes.pointer(g), ctypes.c_void_p), b"extern \"C\" __global__ void k(){}")
+    assert not h
+    assert "tkm_codegen_cuda_string" in R.last_error()

@@ -9,7 +9,7 @@ if the library is missing or a call fails, an exception is raised.
 import ctypes
 import os
 
-__all__ = ["lib", "lib_path", "TkbError", "DTYPE_F32", "DTYPE_BF16", "DTYPE_F16"]
+__all__ = ["lib", "lib_path", "engine", "engine_path", "TkbError", "DTYPE_F32", "DTYPE_BF16", "DTYPE_F16"]
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 
@@ -67,6 +67,26 @@ def lib():
             fn.restype = res
         _LIB = L
     return _LIB
+
+
+_ENGINE = None
+
+
+def engine_path():
+    return os.path.join(_HERE, "libtkm.so")
+
+
+def engine():
+    """Load libtkm.so, the Tokamak engine of include/tkm.h (raises if missing).
+    Signatures are declared by the callers (tests/tkm_abi.py, tokamak_b200.runtime)."""
+    global _ENGINE
+    if _ENGINE is None:
+        lib()  # libtkm.so links libtkm_b200.so
+        path = engine_path()
+        if not os.path.exists(path):
+            raise TkbError(f"{path} is missing: build it with __graft_entry__.build()")
+        _ENGINE = ctypes.CDLL(path)
+    return _ENGINE
 
 
 def check(rc, what=""):
