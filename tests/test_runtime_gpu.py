@@ -82,12 +82,14 @@ def test_llama_c1_fp32_step_matches_oracle():
     rt_mod = runtime_mod()
     rng = np.random.default_rng(7)
     rt, orc, params, ref, worst = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_F32, rng, 1e-4, 1e-4, 1e-4)
-    # one SGD step (lr 0.05) moves every weight as the reference's SGD does
+    # the lr-0 step above still accumulated SGD momentum (as the reference
+    # does); the next step (lr 0.05) moves every weight as the reference's SGD
+    _, vel = orc.sgd_update(ref["grads"], 0.0)
     x = rng.normal(0.0, 1.0, rt.input_elements).astype(np.float32)
     y = rng.integers(0, C1["vocab"], C1["batch"] * C1["seq"]).astype(np.int32)
     ref = orc.run(x.astype(np.float64), y)
     rt.step(x, y, 0.05)
-    new_p, _ = orc.sgd_update(ref["grads"], 0.05)
+    new_p, _ = orc.sgd_update(ref["grads"], 0.05, vel)
     got = rt_mod.tkm1_unpack(rt.save_weights())
     for t in range(len(new_p)):
         if t in ref["grads"]:
