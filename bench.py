@@ -1,14 +1,25 @@
-"""Benchmark of the hot path: GQA attention forward + backward, bf16, causal,
-B=8, H=16, S=4096, D=128 (headline shape) through the
-C ABI of libtkm_b200.so.
+"""Benchmark of the hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload attention|train|rows|longctx]
 
-One step = tkb_gqa_attn_fwd + tkb_gqa_attn_bwd over one batch.  Under torchrun
-each rank runs the same per-GPU workload on its own GPU (weak scaling: the
-(batch, head) units are independent, no collective on the data path); the
-timed region is bracketed by barriers and synchronizes, and the elapsed time
-is the max over ranks.  Rank 0 prints one JSON line.
+attention (default; BASELINE.json configs[1], headline shape): GQA attention
+  forward + backward, bf16, causal, B=8, H=16, S=4096, D=128, through the C ABI
+  of libtkm_b200.so.  One step = tkb_gqa_attn_fwd + tkb_gqa_attn_bwd.  Under
+  torchrun every rank runs the same per-GPU workload (weak scaling, no
+  collective on the data path).
+train: one training step of the ~1B Llama-style decoder through
+  the engine API of libtkm.so (bf16, batch 8 x 2048 tokens per GPU), the step
+  captured as one CUDA graph; with N > 1 ranks the gradients are averaged by
+  one NCCL all-reduce inside the graph (data parallel, weak scaling).
+rows: the engine's generated plasma kernels (residual add, RMSNorm,
+  SwiGLU epilogue) and the softmax cross-entropy at the configuration's shapes,
+  timed per launch inside a training step; reported in HBM GB/s.
+longctx: long-context GQA attention fwd+bwd, B=1, 64/8 heads,
+  D=128, causal, S=16384 (or --seq 32768); KV-head groups sharded over ranks.
+
+The timed region is bracketed by barriers and synchronizes, timed with CUDA
+events on the launching stream, max over ranks.  Rank 0 prints one JSON line.
 """
 import argparse
 import json
@@ -129,7 +140,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="attention", choices=["attention", "train", "rows", "longctx"])
+    ap.add_argument("--seq", type=int, default=None, help="sequence length of the longctx / train workloads")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per GPU of the train workload")
+    ap.add_argument("--profile", default=None, help="write the per-launch profile (train/rows) to this JSON file")
     args = ap.parse_args()
+    if args.workload != "attention":
+        return {"train": run_train, "rows": run_rows, "longctx": run_longctx}[args.workload](args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -296,6 +313,329 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+# ----------------------------------------------------------------- helpers
+
+
+def dist_setup():
+    """(world, rank, local, device); NCCL process group for N > 1."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return world, rank, local, torch.device("cuda", local)
+
+
+def dist_max(value, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def dist_barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def dist_done(world):
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------- train (C4)
+
+
+def train_cpu_baseline(cfg):
+    """The engine step on the host: the float64 graph oracle (a restatement of
+    the reference's semantics, numpy with the attention in the C oracle) on a
+    bounded slice of configuration 4 -- the same layer shapes, one layer, one
+    sequence of 256 tokens, vocabulary 32000."""
+    import numpy as np
+    from oracle.graph_oracle import oracle_for, reference_front_end
+    from oracle.tkm_abi import bind
+    from tokamak_b200 import configs, engine
+    import oracle
+    c = dict(cfg, layers=1, seq=256, batch=1)
+    orc = oracle_for(configs.dsl_for(c), 1, reference_front_end() or bind(engine()))
+    rng = np.random.default_rng(0)
+    orc.set_params([rng.normal(0, 0.02, n) if k == 0 else (np.ones(n) if k == 1 else np.zeros(n))
+                    for _, k, n in orc.tensors])
+    x = rng.normal(0, 1, orc.rows(0) * orc.C[0])
+    y = rng.integers(0, c["vocab"], c["seq"]).astype(np.int32)
+    t0 = time.perf_counter()
+    orc.run(x, y)
+    dt = time.perf_counter() - t0
+    return c["seq"] / dt, oracle.num_threads(), \
+        f"1 layer of configuration 4 (d 2048, GQA 32/8x64, FFN 5632, vocab 32000), 1 x 256 tokens, fwd+bwd, float64"
+
+
+def run_train(args):
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from tokamak_b200 import configs, runtime
+    world, rank, local, dev = dist_setup()
+    cfg = dict(configs.C4)
+    if args.seq:
+        cfg["seq"] = args.seq
+    if args.batch:
+        cfg["batch"] = args.batch
+    B, T, d, V = cfg["batch"], cfg["seq"], cfg["d_model"], cfg["vocab"]
+    rt = runtime.Runtime.from_dsl(configs.dsl_for(cfg), B, runtime.DTYPE_BF16)
+    rt.init_weights(1234, 0.02)
+    if world > 1:
+        obj = [runtime.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        rt.init_dp(obj[0], rank, world)
+    # synthetic tokens: rows are the embeddings of uniform token ids (a
+    # seeded N(0, 0.02) table), labels the next token
+    g = np.random.default_rng(100 + rank)
+    table = g.normal(0.0, 0.02, (V, d)).astype(np.float32)
+    tokens = g.integers(0, V, (B, T + 1))
+    x = torch.from_numpy(table[tokens[:, :-1]].reshape(-1)).pin_memory()
+    y = torch.from_numpy(tokens[:, 1:].reshape(-1).astype(np.int32)).pin_memory()
+    L = runtime.lib()
+    lr = 1e-4
+
+    def step_e2e():
+        loss = L.tkm_runtime_step_i32(rt.h, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()), lr)
+        if not np.isfinite(loss):
+            raise RuntimeError("train step failed: " + runtime.last_error())
+        return loss
+
+    first = step_e2e()  # uploads this rank's batch, runs eagerly, captures the step graph
+    stream = torch.cuda.ExternalStream(rt.stream)
+    for _ in range(max(0, args.warmup - 1)):
+        rt.step_resident(lr)
+    dist_barrier(world)
+    stream.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_barrier(world)
+    e0.record(stream)
+    for _ in range(args.steps):
+        rt.step_resident(lr)
+    e1.record(stream)
+    stream.synchronize()
+    dist_barrier(world)
+    clocks = sampler.stop()
+    ms = dist_max(e0.elapsed_time(e1), world)
+    # end to end: pinned host embeddings + labels uploaded every step, loss read back
+    e2e_steps = max(2, min(args.steps, 4))
+    dist_barrier(world)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    last = first
+    for _ in range(e2e_steps):
+        last = step_e2e()
+    t1.record(stream)
+    stream.synchronize()
+    e2e_ms = dist_max(t0.elapsed_time(t1) / e2e_steps, world)
+    tokens_step = B * T
+    value = tokens_step * world * args.steps / (ms * 1e-3)
+    e2e_value = tokens_step * world / (e2e_ms * 1e-3)
+    prof = None
+    if rank == 0 and args.profile:
+        prof = rt.profile(iters=2)
+        with open(args.profile, "w") as f:
+            json.dump(prof, f)
+    # model FLOPs of one step: every GEMM (forward 2, backward 4 per MAC) plus attention
+    L_, q, kv, hd, F = cfg["layers"], cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["ffn"]
+    gemm_macs = L_ * d * (q * hd + 2 * kv * hd + q * hd + 3 * F) + d * V
+    attn = L_ * 4.0 * B * q * T * T * hd * 0.5 * 3.5
+    step_flops = 6.0 * tokens_step * gemm_macs + attn
+    peak, peak_sus, hbm, src = load_peaks()
+    achieved = step_flops / (ms / args.steps * 1e-3) / 1e12
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu_baseline:
+            try:
+                v, cores, sample = train_cpu_baseline(cfg)
+                cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+            except Exception as e:
+                cpu = {"value": None, "unit": "tokens/s", "cores": None, "kind": "port", "sample": f"failed: {e}"}
+        line = {
+            "metric": "train tokens/sec (Llama-style ~1B, bf16, data parallel)", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded uniform token ids, N(0,0.02) embeddings and weights)",
+            "config": {"workload": "llama_1b_train_step", "layers": L_, "d_model": d, "heads": f"{q}/{kv}x{hd}",
+                       "ffn": F, "vocab": V, "seq_len": T, "micro_batch": B, "global_batch": B * world,
+                       "parallelism": f"dp{world}", "graph": "whole step captured as one CUDA graph",
+                       "l2": "working set far above L2 (activations ~40 GB)"},
+            "loss_first_step": first, "loss_last": last,
+            "roofline": {"bound": "tensor", "kernel": "whole step (GEMM + attention FLOPs)", "achieved": achieved,
+                         "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
+                         "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json)", "traffic": None,
+                         "flops_per_step": step_flops},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 4 + y.numel() * 4,
+                    "d2h_bytes_per_step": 4, "path": "pinned host -> tkm_runtime_step_i32 (engine C API) -> loss"},
+            "cpu_baseline": cpu, "gpu_launches": None, "clocks": clocks,
+        }
+        if prof:
+            by_kind = {}
+            for e in prof:
+                by_kind[e["kind"]] = by_kind.get(e["kind"], 0.0) + e["ms"]
+            line["profile_ms_by_kind"] = by_kind
+            line["gpu_launches"] = len(prof)
+        print(json.dumps(line))
+    rt.close()
+    dist_done(world)
+    return 0
+
+
+# ------------------------------------------------------------- rows (C3)
+
+
+def run_rows(args):
+    """Generated plasma kernels at configuration 2's shapes, timed per launch
+    by the engine's profiler inside a bf16 training step of the graph
+    [16384 x 4096] -> FC -> Bias+Add(residual) -> RMSNorm -> twin FC(11008)
+    -> Bias+SiLU * Bias -> FC, and the softmax cross-entropy over
+    [8192 x 32000] logits."""
+    from tokamak_b200 import runtime
+    world, rank, local, dev = dist_setup()
+    chain = """input: 1x16384x4096
+flow:
+  r: {
+    branch: FC(4096)
+    skip: Identity
+  } -> Add
+  f: RMSNorm -> {
+    gate: FC(11008) -> SiLU
+    up: FC(11008)
+  } -> Mul -> FC(10) -> SoftmaxCE
+"""
+    ce = """input: 1x8192x512
+flow:
+  h: FC(32000) -> SoftmaxCE
+"""
+    import numpy as np
+    out = []
+    for dsl in (chain, ce):
+        rt = runtime.Runtime.from_dsl(dsl, 1, runtime.DTYPE_BF16)
+        rt.init_weights(7, 0.02)
+        x = np.random.default_rng(1).normal(0, 1, rt.input_elements).astype(np.float32)
+        rt.step(x, None, 0.0)
+        prof = rt.profile(iters=max(3, args.steps))
+        out += [e for e in prof if e["kind"] in ("plasma", "softmax/loss")]
+        rt.close()
+    peak, peak_sus, hbm, src = load_peaks()
+    rows = []
+    for e in out:
+        gbs = e["bytes"] / (e["ms"] * 1e-3) / 1e9
+        rows.append({"name": e["name"], "ms": e["ms"], "bytes": e["bytes"], "GB/s": gbs, "frac": gbs / hbm})
+    tot_b = sum(r["bytes"] for r in rows)
+    tot_ms = sum(r["ms"] for r in rows)
+    agg = tot_b / (tot_ms * 1e-3) / 1e9
+    dom = max(rows, key=lambda r: r["ms"])
+    if args.profile and rank == 0:
+        with open(args.profile, "w") as f:
+            json.dump(rows, f, indent=1)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "fused row kernels achieved HBM GB/s (bf16)", "value": agg * world, "unit": "GB/s",
+            "n_gpus": world, "steps": max(3, args.steps), "warmup": 1, "ms_per_step": tot_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "plasma_rows", "shapes": "16384x4096 add+RMSNorm, 16384x11008 SwiGLU, 8192x32000 CE",
+                       "l2": "every tensor larger than L2"},
+            "kernels": rows,
+            "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": dom["GB/s"], "peak": hbm, "unit": "GB/s",
+                         "frac": dom["GB/s"] / hbm, "peak_source": f"{src} HBM copy (MEASURED_PEAKS.json)",
+                         "traffic": None},
+            "e2e": None, "cpu_baseline": None, "gpu_launches": len(rows)}))
+    dist_done(world)
+    return 0
+
+
+# ---------------------------------------------------------- longctx (C5)
+
+
+def run_longctx(args):
+    import ctypes
+
+    import torch
+
+    from tokamak_b200 import lib, ops
+    world, rank, local, dev = dist_setup()
+    S = args.seq or 16384
+    Hq_all, Hkv_all, D = 64, 8, 128
+    if Hkv_all % world:
+        raise SystemExit("KV-head groups (8) must divide over the ranks")
+    Hkv = Hkv_all // world
+    Hq = Hq_all // world
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    qkv = torch.randn(1, S, (Hq + 2 * Hkv) * D, device=dev, generator=g).to(torch.bfloat16)
+    dout = torch.randn(1, S, Hq * D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(1, S, Hq * D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(Hq, S, dtype=torch.float32, device=dev)
+    dqkv = torch.empty_like(qkv)
+    L = lib()
+    ws_bytes = L.tkb_gqa_attn_bwd_workspace(1, S, Hq, D, 1)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    sc = D ** -0.5
+    sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), 1, S, Hq, Hkv, D, sc, 1, 1, sp), "fwd")
+        ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(dqkv), P(ws), ws_bytes, 1, S, Hq, Hkv, D,
+                                     sc, 1, 1, sp), "bwd")
+
+    for _ in range(args.warmup):
+        step()
+    dist_barrier(world)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    n0 = L.tkb_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist_barrier(world)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    dist_barrier(world)
+    clocks = sampler.stop()
+    ms = dist_max(e0.elapsed_time(e1), world)
+    f, b = attn_flops(1, Hq, S, D, True)
+    value = (f + b) * world * args.steps / (ms * 1e-3) / 1e12
+    peak, peak_sus, hbm, src = load_peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "long-context GQA attn fwd+bwd TFLOP/s (bf16, causal)", "value": value, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "gqa_attention_long_context", "B": 1, "Hq": Hq_all, "Hkv": Hkv_all, "S": S, "D": D,
+                       "causal": True, "per_gpu": f"{Hq} query / {Hkv} KV heads",
+                       "parallelism": f"KV-head groups sharded x{world} (no collective)"},
+            "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
+                         "frac": value / world / peak, "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
+                         "traffic": None},
+            "e2e": None, "cpu_baseline": None, "gpu_launches": int(L.tkb_launch_count() - n0), "clocks": clocks}))
+    dist_done(world)
     return 0
 
 

@@ -275,6 +275,29 @@ TKM_API const char *tkm_last_error(void);
 TKM_API int tkm_nccl_unique_id(void *out128);
 TKM_API int tkm_runtime_init_dp(TkmRuntime *rt, const void *unique_id128, int rank, int world_size);
 
+/* Per-launch device timing of the training step: runs `iters` eager steps
+ * (weights are updated with the current learning rate), timing every launch
+ * of the step with CUDA events, and fills up to `capacity` entries in step
+ * order with average milliseconds and the launch's algorithmic work.
+ * kind: 0 plasma group, 1 GEMM, 2 attention, 3 softmax / loss, 4 SGD,
+ * 5 collective.  Returns the number of entries. */
+typedef struct {
+    char name[64];
+    int node, kind, backward;
+    double bytes, flops;
+    float ms;
+} TkmProfileEntry;
+TKM_API int tkm_runtime_profile(TkmRuntime *rt, int iters, TkmProfileEntry *out, int capacity);
+
+/* Re-draws every learnable tensor on the device: GEMM weights N(0, std)
+ * (std <= 0 keeps the He scale sqrt(2 / fan_in) the engine starts with),
+ * gains 1, biases and shifts 0; velocities are cleared. */
+TKM_API int tkm_runtime_init_weights(TkmRuntime *rt, unsigned long long seed, float std);
+
+/* The runtime's CUDA stream (a cudaStream_t), for callers that time or order
+ * their own work against it. */
+TKM_API void *tkm_runtime_stream(const TkmRuntime *rt);
+
 #ifdef __cplusplus
 }
 #endif

@@ -202,7 +202,12 @@ def test_fused_twin_user_fluid_graph():
             lm = rt.step(xm, y, 0.0)
             rt.step(x, y, 0.0)
             ana = rt.grad_sample(0, i)
-            assert abs(ana - (lp - lm) / (2 * eps)) <= 1e-2, (dtype, i)
+            # the reference's 1e-2 holds in fp32; bf16 activations (8-bit
+            # mantissa, coarser than the reference's fp16) round the loss
+            # values themselves to ~1e-3, so the central difference carries
+            # ~2e-2 of noise there
+            tol = 1e-2 if dtype == rt_mod.DTYPE_F32 else 5e-2
+            assert abs(ana - (lp - lm) / (2 * eps)) <= tol, (dtype, i)
         if dtype == rt_mod.DTYPE_F32:
             orc = oracle_for(dsl, 4)
             orc.set_params([p.astype(np.float64) for p in rt_mod.tkm1_unpack(rt.save_weights())])

@@ -207,9 +207,14 @@ int tkb_sgd_step(const tkb_sgd_tensor* table, int n_tensors, const float* lr, fl
   if (!table || n_tensors <= 0 || !lr) return fail(TKB_ERR_ARG, "tkb_sgd_step: bad arguments");
   static_assert(sizeof(tkb_sgd_tensor) == sizeof(SgdTensor), "SGD record layout");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int gy = n_tensors < 65535 ? n_tensors : 65535;
-  sgd_kernel<<<dim3(64, gy), 256, 0, st>>>(reinterpret_cast<const SgdTensor*>(table), n_tensors, lr, momentum,
-                                           weight_decay, seed);
+  if (n_tensors <= SGD_MAXT) {
+    sgd_kernel<<<148 * 8, 256, 0, st>>>(reinterpret_cast<const SgdTensor*>(table), n_tensors, lr, momentum,
+                                        weight_decay, seed);
+  } else {
+    const int gy = n_tensors < 65535 ? n_tensors : 65535;
+    sgd_kernel_many<<<dim3(64, gy), 256, 0, st>>>(reinterpret_cast<const SgdTensor*>(table), n_tensors, lr,
+                                                  momentum, weight_decay, seed);
+  }
   return cuda_status(cudaGetLastError(), "tkb_sgd_step", 1);
 }
 

@@ -123,6 +123,27 @@ TKB_DEVFN float block_max(float v, float* sh) {
   return warp_max(t);
 }
 
+// Block-wide reductions for an NTH-thread block (NTH a multiple of 32, <= 1024).
+template <int NTH>
+TKB_DEVFN float block_sum_n(float v, float* sh) {
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane_id() == 0) sh[warp_id()] = v;
+  __syncthreads();
+  float t = lane_id() < NTH / 32 ? sh[lane_id()] : 0.f;
+  return warp_sum(t);
+}
+
+template <int NTH>
+TKB_DEVFN float block_max_n(float v, float* sh) {
+  v = warp_max(v);
+  __syncthreads();
+  if (lane_id() == 0) sh[warp_id()] = v;
+  __syncthreads();
+  float t = lane_id() < NTH / 32 ? sh[lane_id()] : -INFINITY;
+  return warp_max(t);
+}
+
 static int row_grid(int rows, int per_sm) {
   const int cap = 148 * per_sm;
   return rows < cap ? (rows < 1 ? 1 : rows) : cap;
@@ -491,8 +512,8 @@ __global__ void __launch_bounds__(NT) qkv_prep_bwd_kernel(const T* __restrict__ 
 
 // ============================================================ softmax and softmax losses
 // Row kept in registers: MAXV vectors of VEC per thread (C <= NT*VEC*MAXV).
-template <typename T, int VEC, int MAXV>
-__global__ void __launch_bounds__(NT) softmax_fwd_kernel(const T* __restrict__ x, T* __restrict__ p, int rows, int C) {
+template <typename T, int VEC, int MAXV, int NTH>
+__global__ void __launch_bounds__(NTH) softmax_fwd_kernel(const T* __restrict__ x, T* __restrict__ p, int rows, int C) {
   __shared__ float sh[32];
   const int nvec = C / VEC;
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -501,18 +522,18 @@ __global__ void __launch_bounds__(NT) softmax_fwd_kernel(const T* __restrict__ x
     float mx = -INFINITY;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
         ldv<T, VEC>(x + base + vi * VEC, v[i]);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) mx = fmaxf(mx, v[i][e]);
       }
     }
-    mx = block_max(mx, sh);
+    mx = block_max_n<NTH>(mx, sh);
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
@@ -521,10 +542,10 @@ __global__ void __launch_bounds__(NT) softmax_fwd_kernel(const T* __restrict__ x
         }
       }
     }
-    const float inv = 1.0f / block_sum(sum, sh);
+    const float inv = 1.0f / block_sum_n<NTH>(sum, sh);
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) v[i][e] *= inv;
@@ -535,8 +556,8 @@ __global__ void __launch_bounds__(NT) softmax_fwd_kernel(const T* __restrict__ x
 }
 
 // dx += p * (dp - <p, dp>)   (src/tkm_gpu.cu:615-630)
-template <typename T, int VEC, int MAXV>
-__global__ void __launch_bounds__(NT) softmax_bwd_kernel(const T* __restrict__ p, const T* __restrict__ dp,
+template <typename T, int VEC, int MAXV, int NTH>
+__global__ void __launch_bounds__(NTH) softmax_bwd_kernel(const T* __restrict__ p, const T* __restrict__ dp,
                                                          T* __restrict__ dx, int rows, int C) {
   __shared__ float sh[32];
   const int nvec = C / VEC;
@@ -546,7 +567,7 @@ __global__ void __launch_bounds__(NT) softmax_bwd_kernel(const T* __restrict__ p
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
         ldv<T, VEC>(p + base + vi * VEC, pv[i]);
         ldv<T, VEC>(dp + base + vi * VEC, dv[i]);
@@ -554,10 +575,10 @@ __global__ void __launch_bounds__(NT) softmax_bwd_kernel(const T* __restrict__ p
         for (int e = 0; e < VEC; ++e) dot = fmaf(pv[i][e], dv[i][e], dot);
       }
     }
-    dot = block_sum(dot, sh);
+    dot = block_sum_n<NTH>(dot, sh);
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
         float o[VEC];
         ldv<T, VEC>(dx + base + vi * VEC, o);
@@ -572,8 +593,8 @@ __global__ void __launch_bounds__(NT) softmax_bwd_kernel(const T* __restrict__ p
 // Fused softmax loss forward + backward for one row per block
 // (src/tkm_gpu.cu:632-682): kind 0 CE, 1 focal(gamma), 2 Brier.
 // row_loss[row] receives the row's loss contribution already divided by rows.
-template <typename T, int VEC, int MAXV>
-__global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ logits,
+template <typename T, int VEC, int MAXV, int NTH>
+__global__ void __launch_bounds__(NTH) softmax_loss_kernel(const T* __restrict__ logits,
                                                           const int32_t* __restrict__ labels, T* __restrict__ dlogits,
                                                           float* __restrict__ row_loss, int* __restrict__ correct,
                                                           int rows, int C, int kind, float gamma) {
@@ -589,7 +610,7 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
     int arg = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
         ldv<T, VEC>(logits + base + vi * VEC, v[i]);
 #pragma unroll
@@ -607,8 +628,8 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
     __syncthreads();
     if (lane_id() == 0) { sh[warp_id()] = mx; shi[warp_id()] = arg; }
     __syncthreads();
-    mx = lane_id() < NT / 32 ? sh[lane_id()] : -INFINITY;
-    arg = lane_id() < NT / 32 ? shi[lane_id()] : 0x7fffffff;
+    mx = lane_id() < NTH / 32 ? sh[lane_id()] : -INFINITY;
+    arg = lane_id() < NTH / 32 ? shi[lane_id()] : 0x7fffffff;
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) {
       const float om = __shfl_xor_sync(0xffffffffu, mx, m);
@@ -618,7 +639,7 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
     float sum = 0.f, xy = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+      const int vi = threadIdx.x + i * NTH;
       if (vi < nvec) {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
@@ -628,8 +649,8 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
         }
       }
     }
-    sum = block_sum(sum, sh);
-    xy = block_sum(xy, sh);  // exactly one thread holds the label logit
+    sum = block_sum_n<NTH>(sum, sh);
+    xy = block_sum_n<NTH>(xy, sh);  // exactly one thread holds the label logit
     const float inv_sum = 1.0f / sum;
     float pt = expf(xy - mx) * inv_sum;
     pt = fmaxf(pt, 1e-7f);
@@ -639,7 +660,7 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
     if (kind == 2) {
 #pragma unroll
       for (int i = 0; i < MAXV; ++i) {
-        const int vi = threadIdx.x + i * NT;
+        const int vi = threadIdx.x + i * NTH;
         if (vi < nvec) {
 #pragma unroll
           for (int e = 0; e < VEC; ++e) {
@@ -649,8 +670,8 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
           }
         }
       }
-      bdot = block_sum(bdot, sh);
-      brier = block_sum(brier, sh);
+      bdot = block_sum_n<NTH>(bdot, sh);
+      brier = block_sum_n<NTH>(brier, sh);
     }
     if (threadIdx.x == 0) {
       float lr;
@@ -664,7 +685,7 @@ __global__ void __launch_bounds__(NT) softmax_loss_kernel(const T* __restrict__ 
       const float k2 = 2.0f / static_cast<float>(C);
 #pragma unroll
       for (int i = 0; i < MAXV; ++i) {
-        const int vi = threadIdx.x + i * NT;
+        const int vi = threadIdx.x + i * NTH;
         if (vi < nvec) {
           float o[VEC];
 #pragma unroll
@@ -706,25 +727,120 @@ struct SgdTensor {
   int lowp_dtype;    // 1 = bf16, 2 = f16
 };
 
+// One SGD update of element i (the reference's order of operations).
+TKB_DEVFN void sgd_one(float& p, float& v, float g, float lr, float momentum, float wd, int apply_wd) {
+  if (apply_wd) g = fmaf(wd, p, g);
+  v = fmaf(momentum, v, g);
+  p = fmaf(-lr, fmaf(momentum, v, g), p);
+}
+
+TKB_DEVFN void sgd_store_lowp(void* lowp, int dtype, long long i, float p) {
+  if (dtype == 1) reinterpret_cast<__nv_bfloat16*>(lowp)[i] = __float2bfloat16_rn(p);
+  else reinterpret_cast<__half*>(lowp)[i] = __float2half_rn(p);
+}
+
+// The work is cut into chunks of SGD_CHUNK elements over all tensors; blocks
+// take chunks in turn (balanced whatever the tensor sizes) and move 16 bytes
+// per access when the tensor's arrays are 16-byte aligned.
+constexpr int SGD_CHUNK = 4096;
+constexpr int SGD_MAXT = 1024;
+
 __global__ void __launch_bounds__(256) sgd_kernel(const SgdTensor* __restrict__ tensors, int ntensors,
                                                   const float* __restrict__ d_lr, float momentum, float wd,
                                                   uint32_t* __restrict__ d_seed) {
+  __shared__ long long start[SGD_MAXT + 1];
+  const float lr = *d_lr;
+  // chunk prefix over the tensors: warp 0, each lane owns a contiguous segment
+  if (threadIdx.x < 32) {
+    const int seg = (ntensors + 31) / 32, t0 = threadIdx.x * seg;
+    long long run = 0;
+    for (int t = t0; t < t0 + seg && t < ntensors; ++t) run += (tensors[t].n + SGD_CHUNK - 1) / SGD_CHUNK;
+    long long incl = run;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const long long o = __shfl_up_sync(0xffffffffu, incl, m);
+      if (static_cast<int>(threadIdx.x) >= m) incl += o;
+    }
+    long long c = incl - run;
+    for (int t = t0; t < t0 + seg && t < ntensors; ++t) {
+      start[t] = c;
+      c += (tensors[t].n + SGD_CHUNK - 1) / SGD_CHUNK;
+    }
+    if (threadIdx.x == 31) start[ntensors] = incl;
+  }
+  __syncthreads();
+  const long long total = start[ntensors];
+  for (long long ch = blockIdx.x; ch < total; ch += gridDim.x) {
+    int lo = 0, hi = ntensors - 1;  // last tensor whose first chunk is <= ch
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (start[mid] <= ch) lo = mid;
+      else hi = mid - 1;
+    }
+    const SgdTensor T = tensors[lo];
+    const long long base = (ch - start[lo]) * SGD_CHUNK;
+    const long long end = base + SGD_CHUNK < T.n ? base + SGD_CHUNK : T.n;
+    const bool vec = ((reinterpret_cast<uintptr_t>(T.master) | reinterpret_cast<uintptr_t>(T.vel) |
+                       reinterpret_cast<uintptr_t>(T.grad)) & 15) == 0 &&
+                     (!T.lowp || (reinterpret_cast<uintptr_t>(T.lowp) & 7) == 0) && (base & 3) == 0;
+    if (vec) {
+      for (long long i = base + threadIdx.x * 4; i < end; i += 256 * 4) {
+        if (i + 3 < end) {
+          float4 p = *reinterpret_cast<const float4*>(T.master + i);
+          float4 v = *reinterpret_cast<const float4*>(T.vel + i);
+          const float4 g = *reinterpret_cast<const float4*>(T.grad + i);
+          sgd_one(p.x, v.x, g.x, lr, momentum, wd, T.apply_wd);
+          sgd_one(p.y, v.y, g.y, lr, momentum, wd, T.apply_wd);
+          sgd_one(p.z, v.z, g.z, lr, momentum, wd, T.apply_wd);
+          sgd_one(p.w, v.w, g.w, lr, momentum, wd, T.apply_wd);
+          *reinterpret_cast<float4*>(T.master + i) = p;
+          *reinterpret_cast<float4*>(T.vel + i) = v;
+          if (T.lowp) {
+            if (T.lowp_dtype == 1) {
+              const uint2 u = make_uint2(pack2<true>(p.x, p.y), pack2<true>(p.z, p.w));
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(T.lowp) + i) = u;
+            } else {
+              const uint2 u = make_uint2(pack2<false>(p.x, p.y), pack2<false>(p.z, p.w));
+              *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(T.lowp) + i) = u;
+            }
+          }
+        } else {
+          for (long long k = i; k < end; ++k) {
+            float p = T.master[k], v = T.vel[k];
+            sgd_one(p, v, T.grad[k], lr, momentum, wd, T.apply_wd);
+            T.master[k] = p;
+            T.vel[k] = v;
+            if (T.lowp) sgd_store_lowp(T.lowp, T.lowp_dtype, k, p);
+          }
+        }
+      }
+    } else {
+      for (long long k = base + threadIdx.x; k < end; k += 256) {
+        float p = T.master[k], v = T.vel[k];
+        sgd_one(p, v, T.grad[k], lr, momentum, wd, T.apply_wd);
+        T.master[k] = p;
+        T.vel[k] = v;
+        if (T.lowp) sgd_store_lowp(T.lowp, T.lowp_dtype, k, p);
+      }
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0 && d_seed) *d_seed += 0x9E3779B9u;
+}
+
+// Tables longer than SGD_MAXT: one grid row per tensor, grid-stride within it.
+__global__ void __launch_bounds__(256) sgd_kernel_many(const SgdTensor* __restrict__ tensors, int ntensors,
+                                                       const float* __restrict__ d_lr, float momentum, float wd,
+                                                       uint32_t* __restrict__ d_seed) {
   const float lr = *d_lr;
   for (int t = blockIdx.y; t < ntensors; t += gridDim.y) {
     const SgdTensor T = tensors[t];
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < T.n;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
-      float p = T.master[i];
-      float g = T.grad[i];
-      if (T.apply_wd) g = fmaf(wd, p, g);
-      const float v = fmaf(momentum, T.vel[i], g);
-      p = fmaf(-lr, fmaf(momentum, v, g), p);
+      float p = T.master[i], v = T.vel[i];
+      sgd_one(p, v, T.grad[i], lr, momentum, wd, T.apply_wd);
       T.vel[i] = v;
       T.master[i] = p;
-      if (T.lowp) {
-        if (T.lowp_dtype == 1) reinterpret_cast<__nv_bfloat16*>(T.lowp)[i] = __float2bfloat16_rn(p);
-        else reinterpret_cast<__half*>(T.lowp)[i] = __float2half_rn(p);
-      }
+      if (T.lowp) sgd_store_lowp(T.lowp, T.lowp_dtype, i, p);
     }
   }
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && d_seed) *d_seed += 0x9E3779B9u;
@@ -740,6 +856,26 @@ __global__ void __launch_bounds__(256) sgd_kernel(const SgdTensor* __restrict__ 
     else if (_nv <= 8) KERNEL<T, VEC, 8><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                   \
     else if (_nv <= 16) KERNEL<T, VEC, 16><<<GRID, NT, 0, ST>>>(__VA_ARGS__);                 \
     else return cudaErrorInvalidValue;                                                        \
+  } while (0)
+
+// Softmax-style kernels: 256 threads per row up to 1024 vectors per row,
+// 1024 threads above (each thread keeps at most 16 vectors of the row).
+#define TKB_NV_DISPATCH(KERNEL, T, VEC, NTH, NVEC, GRID, ST, ...)                             \
+  do {                                                                                        \
+    const int _nv = ((NVEC) + (NTH)-1) / (NTH);                                               \
+    if (_nv <= 1) KERNEL<T, VEC, 1, NTH><<<GRID, NTH, 0, ST>>>(__VA_ARGS__);                  \
+    else if (_nv <= 2) KERNEL<T, VEC, 2, NTH><<<GRID, NTH, 0, ST>>>(__VA_ARGS__);             \
+    else if (_nv <= 4) KERNEL<T, VEC, 4, NTH><<<GRID, NTH, 0, ST>>>(__VA_ARGS__);             \
+    else if (_nv <= 8) KERNEL<T, VEC, 8, NTH><<<GRID, NTH, 0, ST>>>(__VA_ARGS__);             \
+    else if (_nv <= 16) KERNEL<T, VEC, 16, NTH><<<GRID, NTH, 0, ST>>>(__VA_ARGS__);           \
+    else return cudaErrorInvalidValue;                                                        \
+  } while (0)
+
+#define TKB_WIDE_DISPATCH(KERNEL, T, VEC, C, ROWS, ST, ...)                                   \
+  do {                                                                                        \
+    const int _nvec = (C) / (VEC);                                                            \
+    if (_nvec <= 1024) TKB_NV_DISPATCH(KERNEL, T, VEC, 256, _nvec, row_grid(ROWS, 8), ST, __VA_ARGS__); \
+    else TKB_NV_DISPATCH(KERNEL, T, VEC, 1024, _nvec, row_grid(ROWS, 2), ST, __VA_ARGS__);     \
   } while (0)
 
 template <typename T>
@@ -838,29 +974,30 @@ static cudaError_t qkv_prep_bwd_t(const void* dout, const void* in, const float*
 template <typename T>
 static cudaError_t softmax_fwd_t(const void* x, void* p, int rows, int C, cudaStream_t st) {
   const int grid = row_grid(rows, 8);
-  if (C % 8 == 0) TKB_ROW_DISPATCH(softmax_fwd_kernel, T, 8, C, grid, st, (const T*)x, (T*)p, rows, C);
-  else TKB_ROW_DISPATCH(softmax_fwd_kernel, T, 2, C, grid, st, (const T*)x, (T*)p, rows, C);
+  (void)grid;
+  if (C % 8 == 0) TKB_WIDE_DISPATCH(softmax_fwd_kernel, T, 8, C, rows, st, (const T*)x, (T*)p, rows, C);
+  else TKB_WIDE_DISPATCH(softmax_fwd_kernel, T, 2, C, rows, st, (const T*)x, (T*)p, rows, C);
   return cudaGetLastError();
 }
 
 template <typename T>
 static cudaError_t softmax_bwd_t(const void* p, const void* dp, void* dx, int rows, int C, cudaStream_t st) {
   const int grid = row_grid(rows, 8);
-  if (C % 8 == 0) TKB_ROW_DISPATCH(softmax_bwd_kernel, T, 8, C, grid, st, (const T*)p, (const T*)dp, (T*)dx, rows, C);
-  else TKB_ROW_DISPATCH(softmax_bwd_kernel, T, 2, C, grid, st, (const T*)p, (const T*)dp, (T*)dx, rows, C);
+  (void)grid;
+  if (C % 8 == 0) TKB_WIDE_DISPATCH(softmax_bwd_kernel, T, 8, C, rows, st, (const T*)p, (const T*)dp, (T*)dx, rows, C);
+  else TKB_WIDE_DISPATCH(softmax_bwd_kernel, T, 2, C, rows, st, (const T*)p, (const T*)dp, (T*)dx, rows, C);
   return cudaGetLastError();
 }
 
 template <typename T>
 static cudaError_t softmax_loss_t(const void* logits, const int32_t* labels, void* dlogits, float* loss, int* correct,
                                   float* row_loss, int rows, int C, int kind, float gamma, cudaStream_t st) {
-  const int grid = row_grid(rows, 8);
   if (C % 8 == 0)
-    TKB_ROW_DISPATCH(softmax_loss_kernel, T, 8, C, grid, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
-                     rows, C, kind, gamma);
+    TKB_WIDE_DISPATCH(softmax_loss_kernel, T, 8, C, rows, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
+                      rows, C, kind, gamma);
   else
-    TKB_ROW_DISPATCH(softmax_loss_kernel, T, 2, C, grid, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
-                     rows, C, kind, gamma);
+    TKB_WIDE_DISPATCH(softmax_loss_kernel, T, 2, C, rows, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
+                      rows, C, kind, gamma);
   if (loss) sum_rows_kernel<<<1, 256, 0, st>>>(row_loss, rows, loss);
   return cudaGetLastError();
 }

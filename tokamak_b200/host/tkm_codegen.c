@@ -81,6 +81,14 @@ static int pow2_at_least(int v) {
 
 static int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+static int group_has_norm(const TkmGraph *g, const PlasmaGroup *pg);
+
+/* Rows move in 16-byte chunks of `vp` channel pairs.  A group with a
+ * normalisation needs whole rows in one block (row statistics): up to 1024
+ * threads per row, each owning kch chunks.  Any other group is elementwise
+ * along the row: a row is split over `ncb` column blocks (blockIdx.y) of at
+ * most 256 threads with one chunk per thread, which keeps registers low and
+ * occupancy high.  Small rows pack rpb rows into a 256-thread block. */
 void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *o) {
     memset(o, 0, sizeof(*o));
     o->C = pg->C;
@@ -90,20 +98,19 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
     while (vp > 1 && o->C2 % vp) vp /= 2;
     o->vp = vp;
     o->nch = o->C2 / vp;
-    if (o->nch <= 32) {
-        o->tpr = pow2_at_least(o->nch > 0 ? o->nch : 1);
-        o->kch = 1;
-    } else if (o->nch <= 256) {
-        o->tpr = round_up(o->nch, 32);
-        o->kch = 1;
+    const int nch = o->nch > 0 ? o->nch : 1;
+    o->kch = 1;
+    o->ncb = 1;
+    if (nch <= 32) {
+        o->tpr = pow2_at_least(nch);
+    } else if (group_has_norm(g, pg)) {
+        /* two or more chunks per thread keep 32+ bytes per operand in flight */
+        o->kch = nch >= 64 ? 2 : 1;
+        if ((nch + o->kch - 1) / o->kch > 1024) o->kch = (nch + 1023) / 1024;
+        o->tpr = round_up((nch + o->kch - 1) / o->kch, 32);
     } else {
-        o->kch = (o->nch + 255) / 256;
-        if (o->kch > 4) o->kch = 4;
-        o->tpr = round_up((o->nch + o->kch - 1) / o->kch, 32);
-        if (o->tpr > 1024) {
-            o->kch = (o->nch + 1023) / 1024;
-            o->tpr = round_up((o->nch + o->kch - 1) / o->kch, 32);
-        }
+        o->ncb = (nch + 255) / 256;
+        o->tpr = round_up((nch + o->ncb - 1) / o->ncb, 32);
     }
     o->rpb = o->tpr >= 256 ? 1 : 256 / o->tpr;
     o->threads = o->tpr * o->rpb;
@@ -137,6 +144,15 @@ static void group_lists(const TkmGraph *g, const PlasmaGroup *pg, Lists *L) {
 static uint32_t node_flags(const TkmGraph *g, int id) {
     const TkmOpSpec *sp = tkm_find_spec_by_node(&g->nodes[id]);
     return sp ? sp->res_flags : 0;
+}
+
+static int group_has_norm(const TkmGraph *g, const PlasmaGroup *pg) {
+    if (pg->is_qkv_prep) return 0;
+    Lists L;
+    group_lists(g, pg, &L);
+    for (int i = 0; i < L.n; i++)
+        if (g->nodes[L.ids[i]].cat == CAT_NORM) return 1;
+    return 0;
 }
 
 int tkm_group_params(const TkmGraph *g, const PlasmaGroup *pg, int *node, int *which) {
@@ -206,7 +222,9 @@ int tkm_group_bwd_grid(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes) 
     tkm_row_geom(g, pg, act_bytes, &gm);
     int nodes[64], which[64];
     if (!tkm_group_params(g, pg, nodes, which)) return gm.fwd_grid;
-    const int cap = tkm_sm_count_hint() * (gm.threads <= 256 ? 4 : 2);
+    /* about 2048 resident threads per SM in total */
+    int cap = tkm_sm_count_hint() * (2048 / gm.threads) / gm.ncb;
+    if (cap < tkm_sm_count_hint()) cap = tkm_sm_count_hint();
     return gm.fwd_grid < cap ? gm.fwd_grid : cap;
 }
 
@@ -653,8 +671,8 @@ static void emit_geom_macros(Em *e) {
         const TkmRowGeom *gm = gs[i];
         bprintf(b, i == 0 ? "#if TKM_ACT_BYTES == 2\n" : "#else\n");
         bprintf(b, "#define TKG_VP %d\n#define TKG_NCH %d\n#define TKG_TPR %d\n#define TKG_KCH %d\n#define TKG_RPB %d\n"
-                   "#define TKG_THREADS %d\n",
-                gm->vp, gm->nch, gm->tpr, gm->kch, gm->rpb, gm->threads);
+                   "#define TKG_THREADS %d\n#define TKG_CB %d\n",
+                gm->vp, gm->nch, gm->tpr, gm->kch, gm->rpb, gm->threads, gm->ncb);
     }
     bprintf(b, "#endif\n#define TKG_C2 %d\n#define TKG_ROWS %d\n#define TKG_INV_C ", g2.C2, g2.rows);
     emit_float(b, 1.0 / (double)g2.C);
@@ -662,7 +680,7 @@ static void emit_geom_macros(Em *e) {
 }
 
 static void undef_geom(Buf *b) {
-    bprintf(b, "#undef TKG_VP\n#undef TKG_NCH\n#undef TKG_TPR\n#undef TKG_KCH\n#undef TKG_RPB\n#undef TKG_THREADS\n"
+    bprintf(b, "#undef TKG_VP\n#undef TKG_NCH\n#undef TKG_TPR\n#undef TKG_KCH\n#undef TKG_RPB\n#undef TKG_THREADS\n#undef TKG_CB\n"
                "#undef TKG_C2\n#undef TKG_ROWS\n#undef TKG_INV_C\n#undef TKG_NRB\n");
 }
 
@@ -682,7 +700,8 @@ static void kernel_head(Em *e, const char *name, int row_from_block) {
     Buf *b = e->b;
     bprintf(b, "extern \"C\" __global__ void __launch_bounds__(TKG_THREADS) TKM_KNAME(%s)(\n", name);
     emit_params(e);
-    bprintf(b, " {\n  const int tkm_lr = threadIdx.x %% TKG_TPR;\n");
+    bprintf(b, " {\n  const int tkm_ll = threadIdx.x %% TKG_TPR; (void)tkm_ll;\n"
+               "  const int tkm_lr = tkm_ll + blockIdx.y * TKG_TPR;\n");
     if (row_from_block)
         bprintf(b, "  const int row = blockIdx.x * TKG_RPB + threadIdx.x / TKG_TPR;\n"
                    "  const bool tkm_row_ok = row < TKG_ROWS;\n");
@@ -758,7 +777,7 @@ static void emit_partials(Em *e, int qkv) {
     for (int p = 0; p < np; p++) {
         char acc[24];
         snprintf(acc, sizeof(acc), "tacc_%s_%d", which_name(which[p]), qkv ? 0 : local_of(e, nodes[p]));
-        bprintf(b, "  tkm_block_partial<TKG_VP, TKG_KCH, TKG_TPR, TKG_RPB, TKG_NCH>(%s, %s + ((size_t)%d * gridDim.x + blockIdx.x) * TKG_C2, tkm_pbuf, tkm_lr);\n",
+        bprintf(b, "  tkm_block_partial<TKG_VP, TKG_KCH, TKG_TPR, TKG_RPB, TKG_NCH>(%s, %s + ((size_t)%d * gridDim.x + blockIdx.x) * TKG_C2, tkm_pbuf, tkm_lr, tkm_ll);\n",
                 acc, A(e, KA_PART, -1, 0), p);
     }
 }
@@ -924,17 +943,18 @@ static void emit_qkv_prep(Em *e) {
     bprintf(b, "}\n\n#undef TKG_HD2\n#undef TKG_QK2\n#undef TKG_SEQ\n#undef TKG_CPH\n");
 }
 
-/* finalize: d_param[c] = sum of the partial rows in block order */
+/* finalize: d_param[c] = sum of the partial rows, two fixed-order stages
+ * (stage 1 over segments of rows, stage 2 over the segment sums) */
 static void emit_finalize(Em *e) {
     int nodes[64], which[64];
     const int np = tkm_group_params(e->g, e->pg, nodes, which);
     if (!np) return;
     Buf *b = e->b;
-    bprintf(b, "extern \"C\" __global__ void __launch_bounds__(256) TKM_KNAME(fin)(const float2* __restrict__ part, int nblk");
+    bprintf(b, "extern \"C\" __global__ void __launch_bounds__(256) TKM_KNAME(fin)(float2* __restrict__ part, int nblk, int stage");
     for (int p = 0; p < np; p++) bprintf(b, ", float* __restrict__ d%d", p);
     bprintf(b, ") {\n  float* dst = nullptr;\n  switch (blockIdx.y) {\n");
     for (int p = 0; p < np; p++) bprintf(b, "    case %d: dst = d%d; break;\n", p, p);
-    bprintf(b, "    default: return;\n  }\n  tkm_colsum_pairs(part + (size_t)blockIdx.y * nblk * TKG_C2, nblk, TKG_C2, dst);\n}\n");
+    bprintf(b, "    default: return;\n  }\n  tkm_colsum_pairs(part + (size_t)blockIdx.y * nblk * TKG_C2, nblk, TKG_C2, stage, dst);\n}\n");
 }
 
 /* canonical code of one group (kernel names through TKM_KNAME) */

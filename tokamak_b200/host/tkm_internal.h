@@ -59,6 +59,7 @@ typedef struct {
     int kch;     /* chunks per thread */
     int rpb;     /* rows per block */
     int threads; /* block size */
+    int ncb;     /* column blocks: > 1 splits a row over blockIdx.y (no row statistics) */
     int rows;    /* batch_size * H * W */
     int fwd_grid;
 } TkmRowGeom;

@@ -166,10 +166,12 @@ __device__ __forceinline__ float tkm_group_sum(float v) {
 
 // One partial row of a per-channel parameter gradient for this block: the
 // accumulators of the block's RPB row slots are summed (in slot order) and
-// written to dst[0 .. C2).  With RPB > 1 the geometry has KCH == 1.
+// written to dst over this block's chunks.  lr: the thread's chunk lane in the
+// row (column blocks included), ll: its lane in the block.  With RPB > 1 the
+// geometry has KCH == 1.
 template <int VP, int KCH, int TPR, int RPB, int NCH>
 __device__ __forceinline__ void tkm_block_partial(const float2 (&acc)[KCH][VP], float2* __restrict__ dst,
-                                                  float2* pbuf, int lr) {
+                                                  float2* pbuf, int lr, int ll) {
   if constexpr (RPB == 1) {
 #pragma unroll
     for (int k = 0; k < KCH; ++k) {
@@ -188,7 +190,7 @@ __device__ __forceinline__ void tkm_block_partial(const float2 (&acc)[KCH][VP], 
       for (int q = 0; q < VP; ++q) {
         float2 s = make_float2(0.f, 0.f);
         for (int r = 0; r < RPB; ++r) {
-          const float2 t = pbuf[(r * TPR + lr) * VP + q];
+          const float2 t = pbuf[(r * TPR + ll) * VP + q];
           s.x += t.x;
           s.y += t.y;
         }
@@ -199,17 +201,24 @@ __device__ __forceinline__ void tkm_block_partial(const float2 (&acc)[KCH][VP], 
   }
 }
 
-// dst[2c], dst[2c+1] = sum over nblk partial rows of pair c, in row order.
-// Block: 256 threads = 32 pairs x 8 row slices; grid.x covers the pairs.
-__device__ __forceinline__ void tkm_colsum_pairs(const float2* __restrict__ part, int nblk, int C2,
+// Column sums of a parameter's partial rows part[nblk][C2] (float2 pairs) in
+// two stages, in a fixed order (deterministic):
+//   stage 1, blockIdx.z = segment: rows [16 z, 16 z + 16) are summed into row 16 z;
+//   stage 2: rows 0, 16, 32, ... are summed into dst[2c], dst[2c + 1].
+// Block: 256 threads = 32 pairs x 8 row slices; blockIdx.x covers the pairs.
+#define TKM_COLSUM_SEG 16
+__device__ __forceinline__ void tkm_colsum_pairs(float2* __restrict__ part, int nblk, int C2, int stage,
                                                  float* __restrict__ dst) {
   __shared__ float2 s[8][33];
   const int lane = threadIdx.x & 31, sl = threadIdx.x >> 5;
   const int pair = blockIdx.x * 32 + lane;
   float2 acc = make_float2(0.f, 0.f);
+  const int r0 = stage == 1 ? blockIdx.z * TKM_COLSUM_SEG : 0;
+  const int r1 = stage == 1 ? min(r0 + TKM_COLSUM_SEG, nblk) : nblk;
+  const int step = stage == 1 ? 8 : 8 * TKM_COLSUM_SEG;
   if (pair < C2)
-    for (int b = sl; b < nblk; b += 8) {
-      const float2 v = part[(size_t)b * C2 + pair];
+    for (int r = r0 + (stage == 1 ? sl : sl * TKM_COLSUM_SEG); r < r1; r += step) {
+      const float2 v = part[(size_t)r * C2 + pair];
       acc.x += v.x;
       acc.y += v.y;
     }
@@ -219,8 +228,12 @@ __device__ __forceinline__ void tkm_colsum_pairs(const float2* __restrict__ part
     float2 t = s[0][lane];
 #pragma unroll
     for (int i = 1; i < 8; ++i) { t.x += s[i][lane].x; t.y += s[i][lane].y; }
-    dst[2 * pair] = t.x;
-    dst[2 * pair + 1] = t.y;
+    if (stage == 1) {
+      part[(size_t)r0 * C2 + pair] = t;
+    } else {
+      dst[2 * pair] = t.x;
+      dst[2 * pair + 1] = t.y;
+    }
   }
 }
 
@@ -397,4 +410,33 @@ extern "C" __global__ void __launch_bounds__(256) tkm_f32_to_bf16(const float* _
 extern "C" __global__ void __launch_bounds__(256) tkm_labels_u8(const uint8_t* __restrict__ src, int n_src,
                                                                 int* __restrict__ dst, int rows) {
   for (int i = blockIdx.x * 256 + threadIdx.x; i < rows; i += gridDim.x * 256) dst[i] = i < n_src ? (int)src[i] : 0;
+}
+
+// learnable-tensor initialisation on the device: std > 0 draws N(0, std) from
+// a counter-based generator (splitmix64 of seed and index, Box-Muller), else
+// every value is `constant`
+__device__ __forceinline__ uint64_t tkm_splitmix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+extern "C" __global__ void __launch_bounds__(256) tkm_fill_param(float* __restrict__ p, long long n, uint64_t seed,
+                                                                 float std, float constant) {
+  for (long long i = (blockIdx.x * 256ll + threadIdx.x) * 2; i < n; i += (long long)gridDim.x * 512) {
+    if (std > 0.f) {
+      const uint64_t r = tkm_splitmix64(seed * 0x100000001B3ull + (uint64_t)i);
+      const float u1 = ((float)(r >> 40) + 1.0f) * (1.0f / 16777217.0f);
+      const float u2 = (float)((r >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+      const float m = sqrtf(-2.0f * logf(u1)) * std;
+      float s, c;
+      sincosf(6.283185307f * u2, &s, &c);
+      p[i] = m * c;
+      if (i + 1 < n) p[i + 1] = m * s;
+    } else {
+      p[i] = constant;
+      if (i + 1 < n) p[i + 1] = constant;
+    }
+  }
 }

@@ -47,7 +47,19 @@ _SIGS = {
     "tkm_nccl_unique_id": ([_vp], _i),
     "tkm_runtime_init_dp": ([_vp, _vp, _i, _i], _i),
     "tkm_codegen_cuda_string": ([_vp], _vp),
+    "tkm_runtime_profile": ([_vp, _i, _vp, _i], _i),
+    "tkm_runtime_init_weights": ([_vp, _c.c_ulonglong, _f], _i),
+    "tkm_runtime_stream": ([_vp], _vp),
 }
+
+
+class ProfileEntry(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 64), ("node", ctypes.c_int), ("kind", ctypes.c_int),
+                ("backward", ctypes.c_int), ("bytes", ctypes.c_double), ("flops", ctypes.c_double),
+                ("ms", ctypes.c_float)]
+
+
+PROFILE_KINDS = {0: "plasma", 1: "gemm", 2: "attention", 3: "softmax/loss", 4: "sgd", 5: "collective"}
 
 _BOUND = None
 
@@ -184,6 +196,32 @@ class Runtime:
 
     def eval_current_loss(self):
         return float(lib().tkm_eval_current_loss(self.h))
+
+    def init_weights(self, seed, std):
+        if not lib().tkm_runtime_init_weights(self.h, int(seed), float(std)):
+            raise TkbError("init_weights: " + last_error())
+
+    @property
+    def stream(self):
+        """cudaStream_t of the runtime (as an integer)."""
+        return lib().tkm_runtime_stream(self.h) or 0
+
+    def step_resident(self, lr):
+        """One step on the inputs and labels already on the device (no upload,
+        no loss read-back, no host synchronisation)."""
+        lib().tkm_runtime_step(self.h, None, None, float(lr))
+
+    def profile(self, iters=3, capacity=4096):
+        """Per-launch device times of `iters` eager training steps, as dicts."""
+        arr = (ProfileEntry * capacity)()
+        n = lib().tkm_runtime_profile(self.h, int(iters), ctypes.cast(arr, _vp), capacity)
+        if n <= 0:
+            raise TkbError("profile: " + last_error())
+        out = []
+        for e in arr[:n]:
+            out.append({"name": e.name.decode(), "node": e.node, "kind": PROFILE_KINDS.get(e.kind, "?"),
+                        "backward": bool(e.backward), "bytes": e.bytes, "flops": e.flops, "ms": e.ms})
+        return out
 
     def init_dp(self, uid, rank, world):
         buf = ctypes.create_string_buffer(bytes(uid), 128)
