@@ -517,18 +517,19 @@ def run_rows(args):
     [8192 x 32000] logits."""
     from tokamak_b200 import runtime
     world, rank, local, dev = dist_setup()
-    chain = """input: 1x16384x4096
+    nrows = args.seq or 16384
+    chain = f"""input: 1x{nrows}x4096
 flow:
-  r: {
+  r: {{
     branch: FC(4096)
     skip: Identity
-  } -> Add
-  f: RMSNorm -> {
+  }} -> Add
+  f: RMSNorm -> {{
     gate: FC(11008) -> SiLU
     up: FC(11008)
-  } -> Mul -> FC(10) -> SoftmaxCE
+  }} -> Mul -> FC(10) -> SoftmaxCE
 """
-    ce = """input: 1x8192x512
+    ce = f"""input: 1x{nrows // 2}x512
 flow:
   h: FC(32000) -> SoftmaxCE
 """

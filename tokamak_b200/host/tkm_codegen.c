@@ -117,6 +117,17 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
     o->fwd_grid = (o->rows + o->rpb - 1) / o->rpb;
 }
 
+void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *o) {
+    tkm_row_geom(g, pg, act_bytes, o);
+    if (o->ncb == 1 && o->kch > 1 && o->nch > 32 && group_has_norm(g, pg)) {
+        o->kch = (o->nch + 1023) / 1024;
+        o->tpr = round_up((o->nch + o->kch - 1) / o->kch, 32);
+        o->rpb = o->tpr >= 256 ? 1 : 256 / o->tpr;
+        o->threads = o->tpr * o->rpb;
+        o->fwd_grid = (o->rows + o->rpb - 1) / o->rpb;
+    }
+}
+
 /* ---------------------------------------------------------- node lists */
 
 /* nodes a group's kernels touch: twin left chain, twin right chain, then
@@ -213,19 +224,6 @@ int tkm_group_kargs(const TkmGraph *g, const PlasmaGroup *pg, int bwd, TkmKArg *
         }
     }
     return n;
-}
-
-/* backward grid: blocks loop over row blocks; groups that reduce parameter
- * gradients use a bounded grid so the partial rows stay few */
-int tkm_group_bwd_grid(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes) {
-    TkmRowGeom gm;
-    tkm_row_geom(g, pg, act_bytes, &gm);
-    int nodes[64], which[64];
-    if (!tkm_group_params(g, pg, nodes, which)) return gm.fwd_grid;
-    /* about 2048 resident threads per SM in total */
-    int cap = tkm_sm_count_hint() * (2048 / gm.threads) / gm.ncb;
-    if (cap < tkm_sm_count_hint()) cap = tkm_sm_count_hint();
-    return gm.fwd_grid < cap ? gm.fwd_grid : cap;
 }
 
 /* --------------------------------------------------------- write planning */
@@ -661,11 +659,16 @@ static void emit_params(Em *e) {
 
 static void set_args(Em *e, int bwd) { e->nargs = tkm_group_kargs(e->g, e->pg, bwd, e->args); }
 
-static void emit_geom_macros(Em *e) {
+static void emit_geom_macros(Em *e, int bwd) {
     Buf *b = e->b;
     TkmRowGeom g2, g4;
-    tkm_row_geom(e->g, e->pg, 2, &g2);
-    tkm_row_geom(e->g, e->pg, 4, &g4);
+    if (bwd) {
+        tkm_row_geom_bwd(e->g, e->pg, 2, &g2);
+        tkm_row_geom_bwd(e->g, e->pg, 4, &g4);
+    } else {
+        tkm_row_geom(e->g, e->pg, 2, &g2);
+        tkm_row_geom(e->g, e->pg, 4, &g4);
+    }
     const TkmRowGeom *gs[2] = {&g2, &g4};
     for (int i = 0; i < 2; i++) {
         const TkmRowGeom *gm = gs[i];
@@ -773,7 +776,7 @@ static void emit_partials(Em *e, int qkv) {
     const int np = tkm_group_params(e->g, e->pg, nodes, which);
     if (!np) return;
     Buf *b = e->b;
-    bprintf(b, "  __shared__ float2 tkm_pbuf[TKG_RPB > 1 ? TKG_THREADS * TKG_VP : 1];\n");
+    bprintf(b, "  __shared__ float2 tkm_pbuf[TKG_RPB > 1 ? TKG_THREADS * TKG_KCH * TKG_VP : 1];\n");
     for (int p = 0; p < np; p++) {
         char acc[24];
         snprintf(acc, sizeof(acc), "tacc_%s_%d", which_name(which[p]), qkv ? 0 : local_of(e, nodes[p]));
@@ -966,11 +969,13 @@ static void emit_group_body(const TkmGraph *g, const PlasmaGroup *pg, const TkmG
     e.plan = plan;
     e.b = b;
     group_lists(g, pg, &e.L);
-    emit_geom_macros(&e);
+    emit_geom_macros(&e, 0);
     if (pg->is_qkv_prep) {
         emit_qkv_prep(&e);
     } else {
         emit_plasma_fwd(&e);
+        undef_geom(b);
+        emit_geom_macros(&e, 1);
         emit_plasma_bwd(&e);
     }
     emit_finalize(&e);

@@ -65,6 +65,9 @@ typedef struct {
 } TkmRowGeom;
 
 void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *geom);
+/* backward kernel geometry (one chunk per thread for normalisation rows, which
+ * keep more state per chunk in the backward) */
+void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *geom);
 int tkm_sm_count_hint(void);
 
 /* ------------------------------------------------ plasma kernel arguments
@@ -96,7 +99,6 @@ typedef struct {
 int tkm_group_kargs(const TkmGraph *g, const PlasmaGroup *pg, int bwd, TkmKArg *out);
 /* parameters whose gradients a group reduces, in partial-row order */
 int tkm_group_params(const TkmGraph *g, const PlasmaGroup *pg, int *node, int *which);
-int tkm_group_bwd_grid(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes);
 /* class id of every group (groups with identical generated code share one) */
 int tkm_codegen_classes(const TkmGraph *g, int *class_of);
 /* NULL if every group can be generated, else the reason of the first that cannot */

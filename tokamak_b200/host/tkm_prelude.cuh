@@ -167,8 +167,8 @@ __device__ __forceinline__ float tkm_group_sum(float v) {
 // One partial row of a per-channel parameter gradient for this block: the
 // accumulators of the block's RPB row slots are summed (in slot order) and
 // written to dst over this block's chunks.  lr: the thread's chunk lane in the
-// row (column blocks included), ll: its lane in the block.  With RPB > 1 the
-// geometry has KCH == 1.
+// row (column blocks included), ll: its lane in the block.  pbuf holds
+// THREADS * KCH * VP float2 when RPB > 1.
 template <int VP, int KCH, int TPR, int RPB, int NCH>
 __device__ __forceinline__ void tkm_block_partial(const float2 (&acc)[KCH][VP], float2* __restrict__ dst,
                                                   float2* pbuf, int lr, int ll) {
@@ -183,18 +183,26 @@ __device__ __forceinline__ void tkm_block_partial(const float2 (&acc)[KCH][VP], 
     }
   } else {
 #pragma unroll
-    for (int q = 0; q < VP; ++q) pbuf[threadIdx.x * VP + q] = acc[0][q];
-    __syncthreads();
-    if (threadIdx.x < TPR && lr < NCH) {
+    for (int k = 0; k < KCH; ++k)
 #pragma unroll
-      for (int q = 0; q < VP; ++q) {
-        float2 s = make_float2(0.f, 0.f);
-        for (int r = 0; r < RPB; ++r) {
-          const float2 t = pbuf[(r * TPR + ll) * VP + q];
-          s.x += t.x;
-          s.y += t.y;
+      for (int q = 0; q < VP; ++q) pbuf[(threadIdx.x * KCH + k) * VP + q] = acc[k][q];
+    __syncthreads();
+    if (threadIdx.x < TPR) {
+#pragma unroll
+      for (int k = 0; k < KCH; ++k) {
+        const int ch = lr + k * TPR;
+        if (ch < NCH) {
+#pragma unroll
+          for (int q = 0; q < VP; ++q) {
+            float2 s = make_float2(0.f, 0.f);
+            for (int r = 0; r < RPB; ++r) {
+              const float2 t = pbuf[((r * TPR + ll) * KCH + k) * VP + q];
+              s.x += t.x;
+              s.y += t.y;
+            }
+            dst[ch * VP + q] = s;
+          }
         }
-        dst[lr * VP + q] = s;
       }
     }
     __syncthreads();
@@ -239,7 +247,9 @@ __device__ __forceinline__ void tkm_colsum_pairs(float2* __restrict__ part, int 
 
 // ------------------------------------------------- activation helpers
 
-__device__ __forceinline__ float tkm_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+// logistic function with the hardware exponential and reciprocal (relative
+// error ~1e-6, far below bf16 and within the fp32 mode's 1e-4 budget)
+__device__ __forceinline__ float tkm_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // log(1 + e^x), taken as x above 20 (where the two agree in fp32)
 __device__ __forceinline__ float tkm_softplus20(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
