@@ -456,6 +456,14 @@ def run_train(args):
     tokens_step = B * T
     value = tokens_step * world * args.steps / (ms * 1e-3)
     e2e_value = tokens_step * world / (e2e_ms * 1e-3)
+    # data parallel: every rank must hold the same weights after the steps
+    import hashlib
+    digest = hashlib.sha256(rt.save_weights()).hexdigest()
+    digests = [None] * world
+    if world > 1:
+        dist.all_gather_object(digests, digest)
+    else:
+        digests = [digest]
     prof = None
     if rank == 0 and args.profile:
         prof = rt.profile(iters=2)
@@ -486,6 +494,7 @@ def run_train(args):
                        "parallelism": f"dp{world}", "graph": "whole step captured as one CUDA graph",
                        "l2": "working set far above L2 (activations ~40 GB)"},
             "loss_first_step": first, "loss_last": last,
+            "dp_weights_identical_across_ranks": len(set(digests)) == 1,
             "roofline": {"bound": "tensor", "kernel": "whole step (GEMM + attention FLOPs)", "achieved": achieved,
                          "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
                          "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json)", "traffic": None,
