@@ -134,6 +134,7 @@ def cpu_reference(steps, warmup, sample_heads=None):
 
 
 def main():
+    global B
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -178,6 +179,8 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
+    if args.batch:  # smaller batch for profiler captures; the bench line itself uses B=8
+        B = args.batch
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     qkv = torch.randn(B, S, 3 * H * D, device=dev, generator=g).to(torch.bfloat16)
     dout = torch.randn(B, S, H * D, device=dev, generator=g).to(torch.bfloat16)
