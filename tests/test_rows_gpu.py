@@ -133,7 +133,7 @@ def test_softmax(rng, dtype, rows, C):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("kind", [0, 1, 2])
-@pytest.mark.parametrize("rows,C", [(64, 1024), (5, 32000), (13, 10)])
+@pytest.mark.parametrize("rows,C", [(64, 1024), (5, 32000), (13, 10), (1500, 8192)])
 def test_softmax_loss(rng, dtype, kind, rows, C):
     o = ops()
     x, xn = dev(2 * rng.standard_normal((rows, C)), dtype)

@@ -704,6 +704,137 @@ __global__ void __launch_bounds__(NTH) softmax_loss_kernel(const T* __restrict__
   }
 }
 
+// Streaming variant for wide rows (vocabularies): two passes over the row
+// instead of holding it in registers, so a 256-thread block per row keeps
+// its registers low and eight rows in flight per SM.  Pass 1 keeps per-thread
+// online statistics (running max m, s1 = sum e^(x-m), s2 = sum e^(2(x-m)) for
+// the Brier score, first-index argmax, the label logit); pass 2 re-reads the
+// row (mostly from L2) and writes the gradient.  Same results as
+// softmax_loss_kernel (src/tkm_gpu.cu:632-682).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __restrict__ logits,
+                                                                  const int32_t* __restrict__ labels,
+                                                                  T* __restrict__ dlogits, float* __restrict__ row_loss,
+                                                                  int* __restrict__ correct, int rows, int C, int kind,
+                                                                  float gamma) {
+  constexpr int NTH = 256;
+  __shared__ float shm[NTH / 32], sh1[NTH / 32], sh2[NTH / 32], shx[NTH / 32];
+  __shared__ int sha[NTH / 32];
+  const int nvec = C / VEC;
+  const float inv_rows = 1.0f / static_cast<float>(rows);
+  const bool brier = kind == 2;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+    const long long base = static_cast<long long>(row) * C;
+    const int y = labels ? labels[row] : 0;
+    float m = -INFINITY, s1 = 0.f, s2 = 0.f, xy = 0.f, best = -INFINITY;
+    int arg = 0x7fffffff;
+    for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
+      float v[VEC];
+      ldv<T, VEC>(logits + base + static_cast<long long>(vi) * VEC, v);
+      float vm = v[0];
+      int va = 0;
+#pragma unroll
+      for (int e = 1; e < VEC; ++e)
+        if (v[e] > vm) { vm = v[e]; va = e; }
+      if (vm > best) { best = vm; arg = vi * VEC + va; }
+      if (y >= vi * VEC && y < vi * VEC + VEC) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (vi * VEC + e == y) xy = v[e];
+      }
+      if (vm > m) {
+        const float r = exp2f((m - vm) * 1.4426950408889634f);
+        s1 *= r;
+        s2 *= r * r;
+        m = vm;
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        const float ex = exp2f((v[e] - m) * 1.4426950408889634f);
+        s1 += ex;
+        if (brier) s2 = fmaf(ex, ex, s2);
+      }
+    }
+    // combine the threads' (m, s1, s2), argmax (first index on ties) and label logit
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o), o1 = __shfl_xor_sync(0xffffffffu, s1, o);
+      const float o2 = __shfl_xor_sync(0xffffffffu, s2, o);
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+      xy += __shfl_xor_sync(0xffffffffu, xy, o);
+      const float nm = fmaxf(m, om);
+      const float ra = m == -INFINITY ? 0.f : exp2f((m - nm) * 1.4426950408889634f);
+      const float rb = om == -INFINITY ? 0.f : exp2f((om - nm) * 1.4426950408889634f);
+      s1 = s1 * ra + o1 * rb;
+      s2 = s2 * ra * ra + o2 * rb * rb;
+      m = nm;
+      if (ob > best || (ob == best && oa < arg)) { best = ob; arg = oa; }
+    }
+    __syncthreads();
+    if (lane_id() == 0) {
+      shm[warp_id()] = m;
+      sh1[warp_id()] = s1;
+      sh2[warp_id()] = s2;
+      shx[warp_id()] = xy;
+      sha[warp_id()] = arg;
+      // best is recovered from the argmax's logit below, not stored
+    }
+    __syncthreads();
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NTH / 32; ++w) M = fmaxf(M, shm[w]);
+    float S1 = 0.f, S2 = 0.f, XY = 0.f;
+    int A = 0x7fffffff;
+    float AB = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NTH / 32; ++w) {
+      if (shm[w] != -INFINITY) {
+        const float r = exp2f((shm[w] - M) * 1.4426950408889634f);
+        S1 = fmaf(sh1[w], r, S1);
+        S2 = fmaf(sh2[w], r * r, S2);
+      }
+      XY += shx[w];
+      // the warp maxima are the warp arguments' logits: compare by value, then index
+      const float wb = shm[w];
+      if (wb > AB || (wb == AB && sha[w] < A)) { AB = wb; A = sha[w]; }
+    }
+    const float inv_s = 1.0f / S1;
+    const float py_raw = exp2f((XY - M) * 1.4426950408889634f) * inv_s;
+    const float pt = fmaxf(py_raw, 1e-7f);
+    const float fw = powf(1.0f - pt, gamma);
+    const float fgs = kind == 1 ? fw - gamma * pt * powf(1.0f - pt, gamma - 1.0f) * logf(pt) : 1.0f;
+    const float sum_p2 = S2 * inv_s * inv_s;
+    const float bdot = sum_p2 - py_raw;                 // sum_c p_c (p_c - t_c)
+    const float brier_sum = sum_p2 - 2.0f * py_raw + 1.0f;  // sum_c (p_c - t_c)^2
+    if (threadIdx.x == 0) {
+      float lr;
+      if (kind == 0) lr = -logf(pt) * inv_rows;
+      else if (kind == 1) lr = -fw * logf(pt) * inv_rows;
+      else lr = brier_sum / static_cast<float>(C) * inv_rows;
+      if (row_loss) row_loss[row] = lr;
+      if (correct && A == y) atomicAdd(correct, 1);
+    }
+    if (dlogits) {
+      const float k2 = 2.0f / static_cast<float>(C);
+      for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
+        float v[VEC], o[VEC];
+        ldv<T, VEC>(logits + base + static_cast<long long>(vi) * VEC, v);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float pc = exp2f((v[e] - M) * 1.4426950408889634f) * inv_s, t = (vi * VEC + e == y) ? 1.f : 0.f;
+          float gr;
+          if (kind == 0) gr = pc - t;
+          else if (kind == 1) gr = fgs * (pc - t);
+          else gr = k2 * pc * ((pc - t) - bdot);
+          o[e] = gr * inv_rows;
+        }
+        stv<T, VEC>(dlogits + base + static_cast<long long>(vi) * VEC, o);
+      }
+    }
+  }
+}
+
 // loss += sum(row_loss) in a fixed order (one block).
 __global__ void __launch_bounds__(256) sum_rows_kernel(const float* __restrict__ row_loss, int rows,
                                                        float* __restrict__ loss) {
@@ -992,7 +1123,10 @@ static cudaError_t softmax_bwd_t(const void* p, const void* dp, void* dx, int ro
 template <typename T>
 static cudaError_t softmax_loss_t(const void* logits, const int32_t* labels, void* dlogits, float* loss, int* correct,
                                   float* row_loss, int rows, int C, int kind, float gamma, cudaStream_t st) {
-  if (C % 8 == 0)
+  if (C % 8 == 0 && C >= 8192)
+    softmax_loss_stream_kernel<T, 8><<<row_grid(rows, 8), 256, 0, st>>>((const T*)logits, labels, (T*)dlogits,
+                                                                        row_loss, correct, rows, C, kind, gamma);
+  else if (C % 8 == 0)
     TKB_WIDE_DISPATCH(softmax_loss_kernel, T, 8, C, rows, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
                       rows, C, kind, gamma);
   else
