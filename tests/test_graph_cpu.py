@@ -100,7 +100,13 @@ def our_lib():
 
 
 def all_cases():
+    from tokamak_b200 import configs
     cases = [(k, v) for k, v in DSL.items()]
+    # the benchmark configurations, including the single-layer slices that the
+    # smoke check and the CPU baseline run (written without the loop macro)
+    for name, cfg in (("C1", configs.C1), ("C4", configs.C4)):
+        for layers in (1, 2):
+            cases.append((f"{name}_layers{layers}", configs.dsl_for(dict(cfg, layers=layers, seq=64))))
     for path in sorted(glob.glob(os.path.join(REF_MODELS, "*.tkm"))):
         cases.append((os.path.basename(path), open(path).read()))
     return cases

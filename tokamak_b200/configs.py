@@ -9,28 +9,37 @@ over the vocabulary; FC layers carry biases, as every FC does in the DSL.
 def llama_dsl(layers, d_model, q_heads, kv_heads, head_dim, ffn, vocab, seq, theta, loss=True):
     kv = kv_heads * head_dim
     head = f"  head: RMSNorm -> FC({vocab})" + (" -> SoftmaxCE" if loss else "")
+    body = f"""attention: {{
+  branch: RMSNorm -> {{
+    q: FC({q_heads * head_dim}) -> RoPE(theta={theta})
+    k: FC({kv}) -> RoPE(theta={theta})
+    v: FC({kv})
+  }} -> GQA(q={q_heads}, kv={kv_heads}, d={head_dim}, causal=true) -> FC({d_model})
+  skip: Identity
+}} -> Add
+ffn: {{
+  branch: RMSNorm -> {{
+    gate: FC({ffn}) -> SiLU
+    up: FC({ffn})
+  }} -> Mul -> FC({d_model})
+  skip: Identity
+}} -> Add"""
+    if layers > 1:
+        # the DSL's loop macro repeats a block only for counts above one
+        # (src/tkm_core.c:219-241); a single layer is written out
+        flow = f"  layer x {layers}: {{\n" + _indent(body, 4) + "\n  }"
+    else:
+        flow = _indent(body, 2)
     return f"""input: 1x{seq}x{d_model}
 prng: pcg32
 flow:
-  layer x {layers}: {{
-    attention: {{
-      branch: RMSNorm -> {{
-        q: FC({q_heads * head_dim}) -> RoPE(theta={theta})
-        k: FC({kv}) -> RoPE(theta={theta})
-        v: FC({kv})
-      }} -> GQA(q={q_heads}, kv={kv_heads}, d={head_dim}, causal=true) -> FC({d_model})
-      skip: Identity
-    }} -> Add
-    ffn: {{
-      branch: RMSNorm -> {{
-        gate: FC({ffn}) -> SiLU
-        up: FC({ffn})
-      }} -> Mul -> FC({d_model})
-      skip: Identity
-    }} -> Add
-  }}
+{flow}
 {head}
 """
+
+
+def _indent(text, n):
+    return "\n".join(" " * n + line for line in text.splitlines())
 
 
 # Configuration 1: 2 layers, d_model 256, 4 heads x 64, SwiGLU 688, vocab 1024,

@@ -288,7 +288,8 @@ void tkm_plan_grads(const TkmGraph *g, TkmGradPlan *plan) {
 /* ------------------------------------------------------------ validation */
 
 static int native_op(const TkmNode *n) {
-    return n->cat == CAT_NORM || n->op == OP_ADD || n->op == OP_MUL || n->op == OP_QKNORM || n->op == OP_ROPE;
+    return n->cat == CAT_NORM || n->op == OP_ADD || n->op == OP_MUL || n->op == OP_QKNORM || n->op == OP_ROPE ||
+           n->op == OP_BIAS;
 }
 
 static const char *group_unsupported(const TkmGraph *g, const PlasmaGroup *pg) {
@@ -531,17 +532,20 @@ static void emit_op_fwd(Em *e, const TkmNode *n, const char *arr, int replay) {
         bprintf(b, "          float2 xh = make_float2((%s[k][q].x - st_mean_%d) * st_istd_%d, (%s[k][q].y - st_mean_%d) * st_istd_%d);\n",
                 arr, j, j, arr, j, j);
         if (f & RES_PARAM_WEIGHT)
-            bprintf(b, "          const float2 gm = %s[tid]; xh.x *= gm.x; xh.y *= gm.y;\n", A(e, KA_PARAM, n->id, 0));
+            bprintf(b, "          const float2 gm = tpw_%d[k][q]; xh.x *= gm.x; xh.y *= gm.y;\n", j);
         if (f & RES_PARAM_BETA)
-            bprintf(b, "          const float2 bt = %s[tid]; xh.x += bt.x; xh.y += bt.y;\n", A(e, KA_PARAM, n->id, 1));
+            bprintf(b, "          const float2 bt = tpt_%d[k][q]; xh.x += bt.x; xh.y += bt.y;\n", j);
         bprintf(b, "          %s[k][q] = xh;\n", arr);
         pairs_end(b);
     } else if (n->op == OP_ADD) {
-        chunks_begin(b);
-        bprintf(b, "        float2 br[TKG_VP]; tkm_ld<TKG_VP>(%s, (long long)row * TKG_C2 + tkm_ch * TKG_VP, br);\n"
-                   "        _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) { %s[k][q].x += br[q].x; %s[k][q].y += br[q].y; }\n",
-                A(e, KA_BRANCH, n->id, 0), arr, arr);
-        chunks_end(b);
+        /* the branch row was loaded with the row's other inputs (tbr_j) */
+        bprintf(b, "    _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+                   "      %s[k][q].x += tbr_%d[k][q].x; %s[k][q].y += tbr_%d[k][q].y;\n    }\n",
+                arr, j, arr, j);
+    } else if (n->op == OP_BIAS) {
+        bprintf(b, "    _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+                   "      %s[k][q].x += tpc_%d[k][q].x; %s[k][q].y += tpc_%d[k][q].y;\n    }\n",
+                arr, j, arr, j);
     } else if (n->op == OP_DROP && replay) {
         /* the replay applies the mask the forward saved */
         bprintf(b, "    const float keep = 1.0f - ");
@@ -583,7 +587,7 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
     if (n->cat == CAT_NORM) {
         const int centered = n->op == OP_LN || n->op == OP_BN;
         char gm[48];
-        if (f & RES_PARAM_WEIGHT) snprintf(gm, sizeof(gm), "%s[tid]", A(e, KA_PARAM, n->id, 0));
+        if (f & RES_PARAM_WEIGHT) snprintf(gm, sizeof(gm), "tpw_%d[k][q]", j);
         else snprintf(gm, sizeof(gm), "make_float2(1.f, 1.f)");
         bprintf(b, "    float2 m = make_float2(0.f, 0.f);\n");
         pairs_begin(b);
@@ -608,6 +612,10 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
     } else if (n->op == OP_ADD) {
         /* the branch receives the incoming gradient; the main path keeps it */
         store_array(b, A(e, KA_DBRANCH, n->id, 0), "TKG_C2", "0", dy, e->plan->add_branch_acc[n->id] > 0);
+    } else if (n->op == OP_BIAS) {
+        pairs_begin(b);
+        bprintf(b, "          tacc_b_%d[k][q].x += %s[k][q].x; tacc_b_%d[k][q].y += %s[k][q].y;\n", j, dy, j, dy);
+        pairs_end(b);
     } else {
         snippet_env(e, n, 1);
         pairs_begin(b);
@@ -710,6 +718,44 @@ static void kernel_head(Em *e, const char *name, int row_from_block) {
                    "  const bool tkm_row_ok = row < TKG_ROWS;\n");
 }
 
+/* per-channel parameters of natively emitted operators, loaded once per
+ * thread (its chunks are the same for every row it handles) */
+static void emit_param_preload(Em *e) {
+    for (int i = 0; i < e->L.n; i++) {
+        const TkmNode *n = &e->g->nodes[e->L.ids[i]];
+        const uint32_t f = node_flags(e->g, n->id);
+        const int norm = n->cat == CAT_NORM, bias = n->op == OP_BIAS;
+        if (!norm && !bias) continue;
+        const struct { uint32_t flag; int which; const char *pfx; } want[3] = {
+            {RES_PARAM_WEIGHT, 0, "tpw"}, {RES_PARAM_BETA, 1, "tpt"}, {RES_PARAM_BIAS, 2, "tpc"}};
+        for (int w = 0; w < 3; w++) {
+            if (!(f & want[w].flag)) continue;
+            if (bias && want[w].which != 2) continue;
+            if (norm && want[w].which == 2) continue;
+            bprintf(e->b,
+                    "  float2 %s_%d[TKG_KCH][TKG_VP];\n"
+                    "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\n"
+                    "    const int tkm_ch = tkm_lr + k * TKG_TPR;\n"
+                    "    _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
+                    "      %s_%d[k][q] = tkm_ch < TKG_NCH ? __ldg(&%s[tkm_ch * TKG_VP + q]) : make_float2(0.f, 0.f);\n"
+                    "  }\n",
+                    want[w].pfx, i, want[w].pfx, i, A(e, KA_PARAM, n->id, want[w].which));
+        }
+    }
+}
+
+/* the row's Add branch inputs, loaded together with its other inputs; `skip`
+ * names a local whose operator is not applied (the backward's last one) */
+static void emit_branch_loads(Em *e, int skip) {
+    for (int i = 0; i < e->L.n; i++) {
+        const TkmNode *n = &e->g->nodes[e->L.ids[i]];
+        if (n->op != OP_ADD || i == skip) continue;
+        char name[16];
+        snprintf(name, sizeof(name), "tbr_%d", i);
+        load_array(e->b, name, A(e, KA_BRANCH, n->id, 0), "TKG_C2", "0");
+    }
+}
+
 static void emit_plasma_fwd(Em *e) {
     Buf *b = e->b;
     const Lists *L = &e->L;
@@ -717,10 +763,12 @@ static void emit_plasma_fwd(Em *e) {
     kernel_head(e, "fwd", 1);
     if (range_has_norm(e, 0, L->n)) bprintf(b, "  __shared__ float tkm_red[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
     declare_stats(e);
+    emit_param_preload(e);
     const char *in = A(e, KA_IN, -1, 0);
     if (e->pg->is_twin_epilogue) {
         load_array(b, "txl", in, "(2 * TKG_C2)", "0");
         load_array(b, "txr", in, "(2 * TKG_C2)", "TKG_C2");
+        emit_branch_loads(e, -1);
         for (int i = 0; i < L->nl; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txl", 0);
         for (int i = L->nl; i < L->nl + L->nr; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txr", 0);
         decl_array(b, "tx");
@@ -728,6 +776,7 @@ static void emit_plasma_fwd(Em *e) {
                    "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
     } else {
         load_array(b, "tx", in, "TKG_C2", "0");
+        emit_branch_loads(e, -1);
     }
     for (int i = L->nl + L->nr; i < L->n; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "tx", 0);
     store_array(b, A(e, KA_OUT, -1, 0), "TKG_C2", "0", "tx", 0);
@@ -795,14 +844,20 @@ static void emit_plasma_bwd(Em *e) {
         bprintf(b, "  __shared__ float tkm_red[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n"
                    "  __shared__ float2 tkm_red2[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
     declare_accs(e);
+    emit_param_preload(e);
     bprintf(b, "  for (int tkm_rb = blockIdx.x; tkm_rb < TKG_NRB; tkm_rb += gridDim.x) {\n"
                "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
                "  const bool tkm_row_ok = row < TKG_ROWS;\n");
     declare_stats(e);
     const char *in = A(e, KA_IN, -1, 0);
+    /* every input of the row is requested before any row statistics */
+    const int last = L->n - 1;
+    const int skip = (L->nc > 0 && e->g->nodes[L->ids[last]].cat != CAT_NORM) ? last : -1;
     if (e->pg->is_twin_epilogue) {
         load_array(b, "txl", in, "(2 * TKG_C2)", "0");
         load_array(b, "txr", in, "(2 * TKG_C2)", "TKG_C2");
+        load_array(b, "tg", A(e, KA_DOUT, -1, 0), "TKG_C2", "0");
+        emit_branch_loads(e, skip);
         emit_replay(e, 0, L->nl, "txl", 0);
         emit_replay(e, L->nl, L->nl + L->nr, "txr", 0);
         decl_array(b, "tx");
@@ -810,9 +865,10 @@ static void emit_plasma_bwd(Em *e) {
                    "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
     } else {
         load_array(b, "tx", in, "TKG_C2", "0");
+        load_array(b, "tg", A(e, KA_DOUT, -1, 0), "TKG_C2", "0");
+        emit_branch_loads(e, skip);
     }
     emit_replay(e, L->nl + L->nr, L->n, "tx", 1);
-    load_array(b, "tg", A(e, KA_DOUT, -1, 0), "TKG_C2", "0");
     emit_bwd_range(e, L->nl + L->nr, L->n, "tg");
     const char *din = A(e, KA_DIN, -1, 0);
     if (e->pg->is_twin_epilogue) {
