@@ -357,12 +357,30 @@ typedef struct {
     int nargs;
     char name_buf[8][16];
     int name_next;
+    int acc_smem;   /* parameter-gradient accumulators in shared memory (TKM_ACC) */
+    int param_regs; /* per-channel parameters preloaded into registers (tp*_j) */
+    char pexpr_buf[4][64];
+    int pexpr_next;
 } Em;
 
 static int local_of(const Em *e, int node) {
     for (int i = 0; i < e->L.n; i++)
         if (e->L.ids[i] == node) return i;
     return -1;
+}
+
+static const char *A(Em *e, int kind, int node, int which);
+
+/* a per-channel parameter (which: 0 weight, 1 beta, 2 bias) of node n at the
+ * pair `tid` inside a pairs loop: the preloaded register or a read-only load */
+static const char *pexpr(Em *e, const TkmNode *n, int which) {
+    static const char *pfx[3] = {"tpw", "tpt", "tpc"};
+    char *out = e->pexpr_buf[e->pexpr_next++ & 3];
+    if (e->param_regs)
+        snprintf(out, 64, "%s_%d[k][q]", pfx[which], local_of(e, n->id));
+    else
+        snprintf(out, 64, "__ldg(&%s[tid])", A(e, KA_PARAM, n->id, which));
+    return out;
 }
 
 /* canonical name "a<i>" of an argument of the kernel being emitted */
@@ -532,9 +550,9 @@ static void emit_op_fwd(Em *e, const TkmNode *n, const char *arr, int replay) {
         bprintf(b, "          float2 xh = make_float2((%s[k][q].x - st_mean_%d) * st_istd_%d, (%s[k][q].y - st_mean_%d) * st_istd_%d);\n",
                 arr, j, j, arr, j, j);
         if (f & RES_PARAM_WEIGHT)
-            bprintf(b, "          const float2 gm = tpw_%d[k][q]; xh.x *= gm.x; xh.y *= gm.y;\n", j);
+            bprintf(b, "          const float2 gm = %s; xh.x *= gm.x; xh.y *= gm.y;\n", pexpr(e, n, 0));
         if (f & RES_PARAM_BETA)
-            bprintf(b, "          const float2 bt = tpt_%d[k][q]; xh.x += bt.x; xh.y += bt.y;\n", j);
+            bprintf(b, "          const float2 bt = %s; xh.x += bt.x; xh.y += bt.y;\n", pexpr(e, n, 1));
         bprintf(b, "          %s[k][q] = xh;\n", arr);
         pairs_end(b);
     } else if (n->op == OP_ADD) {
@@ -543,9 +561,9 @@ static void emit_op_fwd(Em *e, const TkmNode *n, const char *arr, int replay) {
                    "      %s[k][q].x += tbr_%d[k][q].x; %s[k][q].y += tbr_%d[k][q].y;\n    }\n",
                 arr, j, arr, j);
     } else if (n->op == OP_BIAS) {
-        bprintf(b, "    _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
-                   "      %s[k][q].x += tpc_%d[k][q].x; %s[k][q].y += tpc_%d[k][q].y;\n    }\n",
-                arr, j, arr, j);
+        pairs_begin(b);
+        bprintf(b, "          const float2 bb = %s; %s[k][q].x += bb.x; %s[k][q].y += bb.y;\n", pexpr(e, n, 2), arr, arr);
+        pairs_end(b);
     } else if (n->op == OP_DROP && replay) {
         /* the replay applies the mask the forward saved */
         bprintf(b, "    const float keep = 1.0f - ");
@@ -587,7 +605,7 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
     if (n->cat == CAT_NORM) {
         const int centered = n->op == OP_LN || n->op == OP_BN;
         char gm[48];
-        if (f & RES_PARAM_WEIGHT) snprintf(gm, sizeof(gm), "tpw_%d[k][q]", j);
+        if (f & RES_PARAM_WEIGHT) snprintf(gm, sizeof(gm), "%s", pexpr(e, n, 0));
         else snprintf(gm, sizeof(gm), "make_float2(1.f, 1.f)");
         bprintf(b, "    float2 m = make_float2(0.f, 0.f);\n");
         pairs_begin(b);
@@ -595,8 +613,8 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
                    "          const float2 gy = %s[k][q], gm = %s;\n"
                    "          const float2 dxh = make_float2(gy.x * gm.x, gy.y * gm.y);\n",
                 j, j, j, j, j, j, dy, gm);
-        if (f & RES_PARAM_WEIGHT) bprintf(b, "          tacc_w_%d[k][q].x += gy.x * xh.x; tacc_w_%d[k][q].y += gy.y * xh.y;\n", j, j);
-        if (f & RES_PARAM_BETA) bprintf(b, "          tacc_beta_%d[k][q].x += gy.x; tacc_beta_%d[k][q].y += gy.y;\n", j, j);
+        if (f & RES_PARAM_WEIGHT) bprintf(b, "          TKM_ACC(tacc_w_%d).x += gy.x * xh.x; TKM_ACC(tacc_w_%d).y += gy.y * xh.y;\n", j, j);
+        if (f & RES_PARAM_BETA) bprintf(b, "          TKM_ACC(tacc_beta_%d).x += gy.x; TKM_ACC(tacc_beta_%d).y += gy.y;\n", j, j);
         if (centered) bprintf(b, "          m.x += dxh.x + dxh.y;\n");
         bprintf(b, "          m.y += dxh.x * xh.x + dxh.y * xh.y;\n");
         pairs_end(b);
@@ -614,7 +632,7 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
         store_array(b, A(e, KA_DBRANCH, n->id, 0), "TKG_C2", "0", dy, e->plan->add_branch_acc[n->id] > 0);
     } else if (n->op == OP_BIAS) {
         pairs_begin(b);
-        bprintf(b, "          tacc_b_%d[k][q].x += %s[k][q].x; tacc_b_%d[k][q].y += %s[k][q].y;\n", j, dy, j, dy);
+        bprintf(b, "          TKM_ACC(tacc_b_%d).x += %s[k][q].x; TKM_ACC(tacc_b_%d).y += %s[k][q].y;\n", j, dy, j, dy);
         pairs_end(b);
     } else {
         snippet_env(e, n, 1);
@@ -622,9 +640,9 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
         bprintf(b, "          float2 dy = %s[k][q];\n", dy);
         if (needs_pre(n)) bprintf(b, "          const float2 pre = tpre_%d[k][q];\n", j);
         else bprintf(b, "          const float2 pre = make_float2(0.f, 0.f); (void)pre;\n");
-        if (f & RES_PARAM_WEIGHT) bprintf(b, "          float2 acc_dw = tacc_w_%d[k][q];\n", j);
-        if (f & RES_PARAM_BETA) bprintf(b, "          float2 acc_dbeta = tacc_beta_%d[k][q];\n", j);
-        if (f & RES_PARAM_BIAS) bprintf(b, "          float2 acc_db = tacc_b_%d[k][q];\n", j);
+        if (f & RES_PARAM_WEIGHT) bprintf(b, "          float2 acc_dw = TKM_ACC(tacc_w_%d);\n", j);
+        if (f & RES_PARAM_BETA) bprintf(b, "          float2 acc_dbeta = TKM_ACC(tacc_beta_%d);\n", j);
+        if (f & RES_PARAM_BIAS) bprintf(b, "          float2 acc_db = TKM_ACC(tacc_b_%d);\n", j);
         if (sp->bwd_expr) {
             bprintf(b, "          dy.x *= ");
             emit_formula(b, sp->bwd_expr, "pre.x");
@@ -634,9 +652,9 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
         } else {
             bprintf(b, "          {\n%s\n          }\n", sp->bwd_cuda);
         }
-        if (f & RES_PARAM_WEIGHT) bprintf(b, "          tacc_w_%d[k][q] = acc_dw;\n", j);
-        if (f & RES_PARAM_BETA) bprintf(b, "          tacc_beta_%d[k][q] = acc_dbeta;\n", j);
-        if (f & RES_PARAM_BIAS) bprintf(b, "          tacc_b_%d[k][q] = acc_db;\n", j);
+        if (f & RES_PARAM_WEIGHT) bprintf(b, "          TKM_ACC(tacc_w_%d) = acc_dw;\n", j);
+        if (f & RES_PARAM_BETA) bprintf(b, "          TKM_ACC(tacc_beta_%d) = acc_dbeta;\n", j);
+        if (f & RES_PARAM_BIAS) bprintf(b, "          TKM_ACC(tacc_b_%d) = acc_db;\n", j);
         bprintf(b, "          %s[k][q] = dy;\n", dy);
         pairs_end(b);
     }
@@ -760,6 +778,8 @@ static void emit_plasma_fwd(Em *e) {
     Buf *b = e->b;
     const Lists *L = &e->L;
     set_args(e, 0);
+    e->acc_smem = 0;
+    e->param_regs = 1;
     kernel_head(e, "fwd", 1);
     if (range_has_norm(e, 0, L->n)) bprintf(b, "  __shared__ float tkm_red[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
     declare_stats(e);
@@ -805,6 +825,10 @@ static void emit_bwd_range(Em *e, int lo, int hi, const char *dy) {
     for (int i = hi - 1; i >= lo; i--) emit_op_bwd(e, &e->g->nodes[e->L.ids[i]], dy);
 }
 
+/* Parameter-gradient accumulators, one per channel pair a thread owns.  In
+ * shared memory (slot (k * VP + q) * THREADS + thread: private to the thread,
+ * conflict-free) they cost no registers, which lets more rows of a wide
+ * normalisation be in flight per SM; very wide rows keep them in registers. */
 static void declare_accs(Em *e) {
     for (int i = 0; i < e->L.n; i++) {
         const uint32_t f = node_flags(e->g, e->L.ids[i]);
@@ -813,10 +837,32 @@ static void declare_accs(Em *e) {
             if (f & flags[w]) {
                 char name[24];
                 snprintf(name, sizeof(name), "tacc_%s_%d", which_name(w), i);
-                decl_array(e->b, name);
-                zero_array(e->b, name);
+                if (e->acc_smem) {
+                    bprintf(e->b, "  __shared__ float2 %s[TKG_KCH * TKG_VP * TKG_THREADS];\n"
+                                  "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
+                                  "    TKM_ACC(%s) = make_float2(0.f, 0.f);\n",
+                            name, name);
+                } else {
+                    decl_array(e->b, name);
+                    zero_array(e->b, name);
+                }
             }
     }
+}
+
+/* shared-memory bytes of the accumulators of the group's backward kernel
+ * (the larger of the two storage types' geometries) */
+static long acc_smem_bytes(Em *e) {
+    int nodes[64], which[64];
+    const int np = tkm_group_params(e->g, e->pg, nodes, which);
+    long worst = 0;
+    for (int ab = 2; ab <= 4; ab += 2) {
+        TkmRowGeom gm;
+        tkm_row_geom_bwd(e->g, e->pg, ab, &gm);
+        const long bytes = (long)np * gm.kch * gm.vp * gm.threads * 8;
+        if (bytes > worst) worst = bytes;
+    }
+    return worst;
 }
 
 /* one partial row of every reduced parameter gradient per block */
@@ -825,12 +871,19 @@ static void emit_partials(Em *e, int qkv) {
     const int np = tkm_group_params(e->g, e->pg, nodes, which);
     if (!np) return;
     Buf *b = e->b;
-    bprintf(b, "  __shared__ float2 tkm_pbuf[TKG_RPB > 1 ? TKG_THREADS * TKG_KCH * TKG_VP : 1];\n");
+    if (!e->acc_smem)
+        bprintf(b, "  __shared__ float2 tkm_pbuf[TKG_RPB > 1 ? TKG_THREADS * TKG_KCH * TKG_VP : 1];\n");
+    else
+        bprintf(b, "  if (TKG_RPB > 1) __syncthreads();\n");
     for (int p = 0; p < np; p++) {
         char acc[24];
         snprintf(acc, sizeof(acc), "tacc_%s_%d", which_name(which[p]), qkv ? 0 : local_of(e, nodes[p]));
-        bprintf(b, "  tkm_block_partial<TKG_VP, TKG_KCH, TKG_TPR, TKG_RPB, TKG_NCH>(%s, %s + ((size_t)%d * gridDim.x + blockIdx.x) * TKG_C2, tkm_pbuf, tkm_lr, tkm_ll);\n",
-                acc, A(e, KA_PART, -1, 0), p);
+        if (e->acc_smem)
+            bprintf(b, "  tkm_block_partial_s<TKG_VP, TKG_KCH, TKG_TPR, TKG_RPB, TKG_NCH, TKG_THREADS>(%s, %s + ((size_t)%d * gridDim.x + blockIdx.x) * TKG_C2, tkm_lr, tkm_ll);\n",
+                    acc, A(e, KA_PART, -1, 0), p);
+        else
+            bprintf(b, "  tkm_block_partial<TKG_VP, TKG_KCH, TKG_TPR, TKG_RPB, TKG_NCH>(%s, %s + ((size_t)%d * gridDim.x + blockIdx.x) * TKG_C2, tkm_pbuf, tkm_lr, tkm_ll);\n",
+                    acc, A(e, KA_PART, -1, 0), p);
     }
 }
 
@@ -839,12 +892,18 @@ static void emit_plasma_bwd(Em *e) {
     const Lists *L = &e->L;
     const int din_acc = e->plan->group_din_acc[e->pg->id] > 0;
     set_args(e, 1);
+    /* measured on the norm and twin backward kernels: accumulators in shared
+     * memory plus parameters in registers beat every other combination */
+    e->acc_smem = acc_smem_bytes(e) <= 64 * 1024;
+    e->param_regs = 1;
+    bprintf(b, e->acc_smem ? "#define TKM_ACC(a) a[(k * TKG_VP + q) * TKG_THREADS + threadIdx.x]\n"
+                           : "#define TKM_ACC(a) a[k][q]\n");
     kernel_head(e, "bwd", 0);
     if (range_has_norm(e, 0, L->n))
         bprintf(b, "  __shared__ float tkm_red[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n"
                    "  __shared__ float2 tkm_red2[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
     declare_accs(e);
-    emit_param_preload(e);
+    if (e->param_regs) emit_param_preload(e);
     bprintf(b, "  for (int tkm_rb = blockIdx.x; tkm_rb < TKG_NRB; tkm_rb += gridDim.x) {\n"
                "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
                "  const bool tkm_row_ok = row < TKG_ROWS;\n");
@@ -886,7 +945,7 @@ static void emit_plasma_bwd(Em *e) {
     }
     bprintf(b, "  }\n");
     emit_partials(e, 0);
-    bprintf(b, "}\n\n");
+    bprintf(b, "}\n#undef TKM_ACC\n\n");
 }
 
 /* QKV prep (reference src/tkm_codegen.c:211-295, rule src/tkm_registry.c:688-770):
@@ -899,6 +958,8 @@ static void emit_qkv_prep(Em *e) {
     const TkmNode *n = &e->g->nodes[e->pg->node_ids[0]];
     const int hd2 = n->head_dim / 2, qk2 = (n->q_c + n->k_c) / 2, S = e->pg->H * e->pg->W;
     const int din_acc = e->plan->group_din_acc[e->pg->id] > 0;
+    e->acc_smem = 0;
+    e->param_regs = 0;
     bprintf(b, "#define TKG_HD2 %d\n#define TKG_QK2 %d\n#define TKG_SEQ %d\n#define TKG_CPH (TKG_HD2 / TKG_VP)\n", hd2, qk2,
             S > 0 ? S : 1);
 

@@ -209,6 +209,30 @@ __device__ __forceinline__ void tkm_block_partial(const float2 (&acc)[KCH][VP], 
   }
 }
 
+// tkm_block_partial for accumulators in shared memory: slot
+// (k * VP + q) * THREADS + thread.  With RPB > 1 the caller has synchronised
+// the block after the last accumulation.
+template <int VP, int KCH, int TPR, int RPB, int NCH, int THREADS>
+__device__ __forceinline__ void tkm_block_partial_s(const float2* acc, float2* __restrict__ dst, int lr, int ll) {
+  if (threadIdx.x >= TPR) return;
+#pragma unroll
+  for (int k = 0; k < KCH; ++k) {
+    const int ch = lr + k * TPR;
+    if (ch < NCH) {
+#pragma unroll
+      for (int q = 0; q < VP; ++q) {
+        float2 s = acc[(k * VP + q) * THREADS + ll];
+        for (int r = 1; r < RPB; ++r) {
+          const float2 t = acc[(k * VP + q) * THREADS + r * TPR + ll];
+          s.x += t.x;
+          s.y += t.y;
+        }
+        dst[ch * VP + q] = s;
+      }
+    }
+  }
+}
+
 // Column sums of a parameter's partial rows part[nblk][C2] (float2 pairs) in
 // two stages, in a fixed order (deterministic):
 //   stage 1, blockIdx.z = segment: rows [16 z, 16 z + 16) are summed into row 16 z;
