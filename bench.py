@@ -186,7 +186,7 @@ def main():
     dout = torch.randn(B, S, H * D, device=dev, generator=g).to(torch.bfloat16)
     sc = D ** -0.5
     L = lib()
-    ws_bytes = L.tkb_gqa_attn_bwd_workspace(B, S, H, D, 1)
+    ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(B, S, H, D, 1, 1)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     out = torch.empty(B, S, H * D, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B * H, S, dtype=torch.float32, device=dev)
@@ -606,7 +606,7 @@ def run_longctx(args):
     lse = torch.empty(Hq, S, dtype=torch.float32, device=dev)
     dqkv = torch.empty_like(qkv)
     L = lib()
-    ws_bytes = L.tkb_gqa_attn_bwd_workspace(1, S, Hq, D, 1)
+    ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(1, S, Hq, D, 1, 1)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     sc = D ** -0.5
     sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)

@@ -63,6 +63,13 @@ int tkb_gqa_attn_fwd(const void *qkv, void *out, float *lse,
 /* Workspace bytes tkb_gqa_attn_bwd needs (per-row Delta and LSE*log2(e), fp32). */
 size_t tkb_gqa_attn_bwd_workspace(int B, int S, int Hq, int D, int dtype);
 
+/* Workspace bytes with which tkb_gqa_attn_bwd keeps every dS tile (16-bit,
+ * B * Hq * tiles * 32 KB; causal stores only the lower triangle of tiles)
+ * and computes dQ as a GEMM over them instead of recomputing S, P and dP.
+ * Equal to tkb_gqa_attn_bwd_workspace when that area would exceed 8 GiB.
+ * Any size between the two selects the recompute path. */
+size_t tkb_gqa_attn_bwd_workspace_ex(int B, int S, int Hq, int D, int causal, int dtype);
+
 /* Replaces k_gqa_flash_attn_tc_bwd<HEAD_DIM> (src/tkm_gpu.cu:440-598),
  * launched at src/tkm_gpu.cu:1389-1403.  Writes all of dqkv (dQ, dK, dV
  * slices; the reference leaves dK/dV wrong, src/tkm_gpu.cu:588-596).

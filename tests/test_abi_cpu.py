@@ -61,6 +61,13 @@ def test_workspace_sizes():
     rows = 8 * 16 * 4096
     assert rows * 2 * 4 <= n < rows * 2 * 4 + 1024
     assert L.tkb_gqa_attn_bwd_workspace(8, 4096, 16, 128, 0) == 0
+    # with dS kept: 32 KB per 128x128 tile, lower triangle of tiles when causal
+    nq = 4096 // 128
+    assert L.tkb_gqa_attn_bwd_workspace_ex(8, 4096, 16, 128, 1, 1) == n + 8 * 16 * nq * (nq + 1) // 2 * 32768
+    assert L.tkb_gqa_attn_bwd_workspace_ex(8, 4096, 16, 128, 0, 1) == n + 8 * 16 * nq * nq * 32768
+    # beyond 8 GiB of dS the minimum workspace is offered (dQ recomputes)
+    assert L.tkb_gqa_attn_bwd_workspace_ex(1, 32768, 64, 128, 1, 1) == L.tkb_gqa_attn_bwd_workspace(1, 32768, 64, 128, 1)
+    assert L.tkb_gqa_attn_bwd_workspace_ex(8, 4096, 16, 128, 1, 0) == 0
     assert L.tkb_add_rmsnorm_bwd_workspace(16384, 4096) > 0
     assert L.tkb_softmax_loss_workspace(8192) >= 8192 * 4
 

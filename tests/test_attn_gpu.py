@@ -46,7 +46,8 @@ CASES = [
 
 @pytest.mark.parametrize("B,S,Hq,Hkv,D,causal", CASES)
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_attn_fwd_bwd_16bit(rng, B, S, Hq, Hkv, D, causal, dtype):
+@pytest.mark.parametrize("keep_ds", [True, False], ids=["dS-GEMM", "recompute"])
+def test_attn_fwd_bwd_16bit(rng, B, S, Hq, Hkv, D, causal, dtype, keep_ds):
     ops = _ops()
     qkv, dout, tq, td = _case(rng, B, S, Hq, Hkv, D, dtype)
     scale = D ** -0.5
@@ -61,7 +62,7 @@ def test_attn_fwd_bwd_16bit(rng, B, S, Hq, Hkv, D, causal, dtype):
     ref_d = oracle.attn_bwd(qkv, ref_o, dout, ref_lse, B, S, Hq, Hkv, D, scale, causal)
     to = torch.from_numpy(ref_o).to("cuda", dtype)
     tl = torch.from_numpy(ref_lse).cuda()
-    dq = ops.gqa_attn_bwd(tq, to, td, tl, B, S, Hq, Hkv, D, scale, causal)
+    dq = ops.gqa_attn_bwd(tq, to, td, tl, B, S, Hq, Hkv, D, scale, causal, keep_ds=keep_ds)
     torch.cuda.synchronize()
     d = dq.float().cpu().numpy().reshape(B, S, Hq + 2 * Hkv, D)
     r = ref_d.reshape(B, S, Hq + 2 * Hkv, D)

@@ -33,6 +33,7 @@ _SIGS = {
     "tkb_launch_count": ([], ctypes.c_ulonglong),
     "tkb_gqa_attn_fwd": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i, _vp], _i),
     "tkb_gqa_attn_bwd_workspace": ([_i, _i, _i, _i, _i], _sz),
+    "tkb_gqa_attn_bwd_workspace_ex": ([_i, _i, _i, _i, _i, _i], _sz),
     "tkb_gqa_attn_bwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _i, _i, _f, _i, _i, _vp], _i),
     "tkb_add_rmsnorm_fwd": ([_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _i, _vp], _i),
     "tkb_add_rmsnorm_bwd_workspace": ([_i, _i], _sz),

@@ -7,7 +7,7 @@
 // heads of each kv head (the reference writes dK := dQ, dV := dO at
 // src/tkm_gpu.cu:588-596) and a correctly laid-out dQ = scale * dS K.
 //
-// Two kernels, no atomics, deterministic:
+// Two kernels, no atomics, deterministic (three with a dS workspace, below):
 //  * attn_bwd_dkdv_kernel: one CTA per 128-key tile of a (batch, kv head);
 //    K, V and the dK, dV accumulators stay resident while the CTA walks every
 //    (query head of the group, 128-row query tile) pair that sees the keys.
@@ -17,6 +17,12 @@
 //    Q, dO and the dQ accumulator resident, K/V blocks streamed.  Three MMAs
 //    per block, M = 128 queries: S = Q K^T, dP = dO V^T, dQ += dS K (dS from
 //    TMEM).
+//  * with a dS workspace the dK/dV kernel also stores dS (16-bit, 32 KB per
+//    128x128 tile) and attn_bwd_dsk_kernel computes dQ = scale * dS K as a
+//    plain tcgen05 GEMM over the stored tiles, in place of the dQ kernel and
+//    its recomputation of S, P and dP.  A tile is kept in the MMA's
+//    no-swizzle core-matrix order (see ds_tile), so that each warp store
+//    writes whole 128-byte lines and the GEMM fetches a tile with one bulk copy.
 // In both kernels warps 0-7 are two compute warpgroups (one thread per TMEM
 // lane/row, each group owning half of the 128 columns), warp 8 issues TMA,
 // warp 9 issues tcgen05.mma.  The MMA order lets the next step's S/dP MMAs
@@ -40,6 +46,15 @@ TKB_DEVFN void wait_ld_dep32(uint32_t (&r)[32]) {
 // Packed 16-bit column in TMEM of K-step kk (16 rows of the reduction dim) when
 // compute warpgroup 0 stores its half at columns [0,32) and group 1 at [64,96).
 TKB_DEVFN uint32_t half_split_col(int kk) { return kk < 4 ? kk * 8 : 64 + (kk - 4) * 8; }
+
+// Index of the dS tile (query tile i, key tile j) within one (batch, q head):
+// causal rows hold only j <= i (lower triangle, row-major), else all nq tiles.
+// Inside a tile, dS[q][k] (16-bit) sits at byte (k / 8) * 2048 + (q / 8) * 128
+// + (k % 8) * 16 + (q % 8) * 2: core matrices of 8 queries x 8 keys (128
+// bytes), 16 consecutive ones along the queries per group of 8 keys.
+TKB_DEVFN long long ds_tile(int i, int j, int nq, bool causal) {
+  return causal ? static_cast<long long>(i) * (i + 1) / 2 + j : static_cast<long long>(i) * nq + j;
+}
 
 // ============================================================================ dK / dV
 template <int D>
@@ -290,6 +305,18 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(ds_ready);
+      if (p.ds) {
+        // key kr of the dS tile (i, jt), this warpgroup's 64 queries: eight
+        // 16-byte core-matrix rows; per store a warp's 32 keys fill four
+        // whole 128-byte core matrices.  Issued while the dK MMA runs.
+        const int hq = g * G + it / n_i;
+        const long long tile = (static_cast<long long>(b) * p.Hq + hq) * p.ds_tiles + ds_tile(i, jt, nq, p.causal);
+        uint8_t* dst = reinterpret_cast<uint8_t*>(p.ds) + tile * 32768 + (kr >> 3) * 2048 + (kr & 7) * 16 + w * 1024;
+        const uint64_t pol = policy_evict_first();  // streamed once: keep Q, dO resident in L2
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          st_global_hint(dst + c * 128, make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]), pol);
+      }
     }
     // epilogue: warpgroup 0 stores dK (scaled), warpgroup 1 stores dV
     if (ok && mbar_wait(kv_done, 0, abort_flag)) {
@@ -576,6 +603,152 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
   }
 }
 
+// ============================================================================ dQ = dS K
+// One CTA per 128-row query tile of a (batch, q head): the stored dS tiles of
+// the row (A, 128 queries x 128 keys in core-matrix order, one bulk copy
+// each) and the matching K tiles (B, TMA, 128-byte swizzle) stream through an
+// NST-stage ring; one thread issues the tcgen05 MMAs into a TMEM
+// accumulator; four warps scale and store dQ.
+template <int D>
+struct DskCfg {
+  static constexpr int SLAB = 128 * 128;
+  static constexpr int TILE_A = 2 * SLAB;       // 128 keys x 128 queries
+  static constexpr int TILE_K = 128 * D * 2;    // 128 keys x D
+  static constexpr int STAGE = TILE_A + TILE_K;
+  static constexpr int NST = (D == 64) ? 4 : 3;
+  static constexpr int OFF_BAR = NST * STAGE;
+  static constexpr int NBAR = 2 * NST + 2;      // full[NST], empty[NST], dq_done, drain
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;
+  static constexpr uint32_t TM_COLS = D;
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_constant__ BwdParams p) {
+  using C = DskCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = full + C::NST;
+  uint64_t* dq_done = empty + C::NST;
+  uint64_t* mma_drain = dq_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int BH = p.B * p.Hq;
+  const int nq = p.S_pad >> 7;
+  const int qt = nq - 1 - static_cast<int>(blockIdx.x / BH);  // longest (causal) first
+  const int bh = blockIdx.x % BH;
+  const int b = bh / p.Hq, h = bh % p.Hq;
+  const int g = h / (p.Hq / p.Hkv);
+  const int nb = p.causal ? qt + 1 : nq;
+  // tiles of one query row are consecutive: tile j of the row at tile0 + j
+  const long long tile0 = static_cast<long long>(bh) * p.ds_tiles + ds_tile(qt, 0, nq, p.causal);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(dq_done, 1);
+    mbar_init(mma_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, C::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&p.tmK);
+      const uint64_t pol_ds = policy_evict_first(), pol_k = policy_evict_last();
+      int issued = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j % C::NST;
+        if (!mbar_wait(&empty[s], ((j / C::NST) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        uint8_t* st = smem + s * C::STAGE;
+        bulk_load_hint(st, reinterpret_cast<const uint8_t*>(p.ds) + (tile0 + j) * 32768, C::TILE_A, &full[s], pol_ds);
+#pragma unroll
+        for (int hh = 0; hh < D / 64; ++hh)
+          tma_load_3d(st + C::TILE_A + hh * C::SLAB, &p.tmK, &full[s], g * D + hh * 64, j * 128, b, pol_k);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        volatile int never = 0;
+        for (int j = max(0, issued - C::NST); j < issued; ++j) mbar_wait(&full[j % C::NST], (j / C::NST) & 1, &never);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id = idesc_f16kind(128, D, BF16, true, true);  // A query-major, B key-major
+      bool ok = true;
+      for (int j = 0; j < nb; ++j) {
+        const int s = j % C::NST;
+        if (!(ok = mbar_wait(&full[s], (j / C::NST) & 1, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t sa = sbase + s * C::STAGE, sk = sa + C::TILE_A;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ss(tmem, sdesc_interleave(sa + kk * 4096, 2048, 128), sdesc_sw128(sk + kk * 2048, C::SLAB, 1024), id,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(dq_done);
+      else {
+        volatile int never = 0;
+        umma_commit(mma_drain);
+        mbar_wait(mma_drain, 0, &never);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue: warps 0-3, one query row each
+    const int r = threadIdx.x;  // TMEM lane
+    const int qrow = qt * 128 + r;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    if (nb > 0 && mbar_wait(dq_done, 0, abort_flag)) {
+      tc_fence_after();
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.dq) +
+                     2 * (static_cast<long long>(b) * p.dkv_batch_stride +
+                          static_cast<long long>(qrow) * p.dkv_row_stride + static_cast<long long>(h) * D);
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_off + c * 32, v);
+        wait_ld_dep32(v);
+        uint4 o[4];
+        uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          ow[e] = pack2<BF16>(__uint_as_float(v[2 * e]) * p.scale, __uint_as_float(v[2 * e + 1]) * p.scale);
+        if (qrow < p.S) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 64);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) d4[e] = o[e];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TM_COLS);
+  }
+}
+
 template <int D, bool BF16>
 static cudaError_t launch_bwd(const BwdParams& p, cudaStream_t stream) {
   {
@@ -585,6 +758,14 @@ static cudaError_t launch_bwd(const BwdParams& p, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(p.B * p.Hkv * (p.S_pad / 128)), 320, C::SMEM, stream>>>(p);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  if (p.ds) {
+    using C = DskCfg<D>;
+    auto kern = attn_bwd_dsk_kernel<D, BF16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    kern<<<static_cast<unsigned>(p.B * p.Hq * (p.S_pad / 128)), 192, C::SMEM, stream>>>(p);
+    return cudaGetLastError();
   }
   {
     using C = DqCfg<D>;

@@ -116,6 +116,29 @@ size_t tkb_gqa_attn_bwd_workspace(int B, int S, int Hq, int D, int dtype) {
   return 2 * round256(rows * 4);
 }
 
+}  // extern "C"
+
+namespace {
+// dS tiles (128 x 128, 16-bit) one (batch, q head) needs: the lower triangle
+// of query x key tiles when causal, else all of them.
+long long ds_tiles_per_head(int S, int causal) {
+  const long long nq = (S + 127) / 128;
+  return causal ? nq * (nq + 1) / 2 : nq * nq;
+}
+// Largest dS area tkb_gqa_attn_bwd_workspace_ex offers (beyond it dQ is
+// recomputed instead of read back).
+constexpr size_t kMaxDsBytes = size_t(8) << 30;
+}  // namespace
+
+extern "C" {
+
+size_t tkb_gqa_attn_bwd_workspace_ex(int B, int S, int Hq, int D, int causal, int dtype) {
+  const size_t base = tkb_gqa_attn_bwd_workspace(B, S, Hq, D, dtype);
+  if (!base) return 0;
+  const size_t ds = static_cast<size_t>(B) * Hq * ds_tiles_per_head(S, causal) * 128 * 128 * 2;
+  return ds <= kMaxDsBytes ? base + ds : base;
+}
+
 int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const float* lse, void* dqkv,
                      void* workspace, size_t workspace_bytes, int B, int S, int Hq, int Hkv, int D, float scale,
                      int causal, int dtype, void* stream) {
@@ -172,6 +195,12 @@ int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const f
   p.causal = causal ? 1 : 0;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
+  // dS path: the workspace holds every dS tile after LSE and Delta
+  const size_t ex = tkb_gqa_attn_bwd_workspace_ex(B, S, Hq, D, causal, dtype);
+  if (ex > need && workspace_bytes >= ex) {
+    p.ds = reinterpret_cast<uint16_t*>(ws + need);
+    p.ds_tiles = ds_tiles_per_head(S, causal);
+  }
   e = attn_bwd_tc(p, D, bf16, st);
   return cuda_status(e, "tkb_gqa_attn_bwd: dK/dV and dQ kernels", 3);
 }

@@ -113,6 +113,22 @@ TKB_DEVFN void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b
       : "memory");
 }
 
+// The same with an L2 cache policy (createpolicy).
+TKB_DEVFN void bulk_load_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t cache_policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(cache_policy)
+      : "memory");
+}
+
+// 16-byte global store with an L2 cache policy.
+TKB_DEVFN void st_global_hint(void* gaddr, uint4 v, uint64_t cache_policy) {
+  asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(gaddr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w), "l"(cache_policy)
+               : "memory");
+}
+
 TKB_DEVFN uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -153,6 +169,18 @@ TKB_DEVFN uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
   d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
   d |= 2ull << 61;
+  return d;
+}
+
+// Shared-memory matrix descriptor without swizzle: the operand is made of
+// 8 x 16-byte core matrices (128 contiguous bytes each); lbo is the byte
+// distance between core matrices adjacent along K, sbo along M/N.
+TKB_DEVFN uint64_t sdesc_interleave(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;
   return d;
 }
 

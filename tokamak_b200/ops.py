@@ -44,13 +44,21 @@ def gqa_attn_fwd(qkv, B, S, Hq, Hkv, D, scale=None, causal=True):
     return out, lse
 
 
-def gqa_attn_bwd(qkv, out, dout, lse, B, S, Hq, Hkv, D, scale=None, causal=True, workspace=None, dqkv=None):
+def gqa_attn_bwd(qkv, out, dout, lse, B, S, Hq, Hkv, D, scale=None, causal=True, workspace=None, dqkv=None,
+                 keep_ds=True):
+    """keep_ds: offer the workspace that stores dS (dQ as a GEMM over it);
+    False gives the minimum workspace, on which dQ recomputes S, P and dP."""
     scale = D ** -0.5 if scale is None else scale
     L = lib()
     dt = dtype_code(qkv)
-    need = L.tkb_gqa_attn_bwd_workspace(B, S, Hq, D, dt)
+    if keep_ds:
+        need = L.tkb_gqa_attn_bwd_workspace_ex(B, S, Hq, D, int(causal), dt)
+    else:
+        need = L.tkb_gqa_attn_bwd_workspace(B, S, Hq, D, dt)
     if workspace is None:
         workspace, _ = _ws(need, qkv.device)
+    else:
+        need = workspace.numel() * workspace.element_size()
     if dqkv is None:
         dqkv = torch.empty_like(qkv)
     check(L.tkb_gqa_attn_bwd(_p(qkv), _p(out), _p(dout), _p(lse), _p(dqkv), _p(workspace), need, B, S, Hq, Hkv,
