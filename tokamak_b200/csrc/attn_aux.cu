@@ -42,41 +42,57 @@ cudaError_t make_tmap_rows(CUtensorMap* m, const void* base, bool bf16, long lon
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-// One warp per (bh, row) of the padded sequence.
+// Rows of the padded sequence are spread over the lanes: D/8 lanes per row
+// (one 16-byte chunk of O and of dO each), 32/(D/8) rows per warp per pass,
+// UNROLL passes with their loads issued before any reduction.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(const void* __restrict__ out, const void* __restrict__ dout,
                                                            const float* __restrict__ lse, float* __restrict__ lse2,
                                                            float* __restrict__ delta, long long o_row_stride, long long o_batch_stride, int B,
                                                            int S, int S_pad, int Hq) {
+  constexpr int LPR = D / 8, RPW = 32 / LPR, UNROLL = 4, ROWS = RPW * UNROLL;
   const long long total = static_cast<long long>(B) * Hq * S_pad;
-  const int lane = threadIdx.x & 31;
-  for (long long wrow = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; wrow < total;
-       wrow += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
-    const long long bh = wrow / S_pad;
-    const int row = static_cast<int>(wrow % S_pad);
-    const int b = static_cast<int>(bh / Hq), h = static_cast<int>(bh % Hq);
-    float acc = 0.f;
-    if (row < S) {
-      const long long off = (static_cast<long long>(b) * o_batch_stride + static_cast<long long>(row) * o_row_stride +
-                             static_cast<long long>(h) * D) * 2;
-      // D 16-bit values = D/8 uint4; lanes take one uint4 each
-      if (lane < D / 8) {
-        const uint4 o = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(out) + off + lane * 16);
-        const uint4 d = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(dout) + off + lane * 16);
-        const uint32_t* ow = reinterpret_cast<const uint32_t*>(&o);
-        const uint32_t* dw = reinterpret_cast<const uint32_t*>(&d);
+  const int lane = threadIdx.x & 31, sub = lane / LPR, chunk = lane % LPR;
+  const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long w0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * ROWS; w0 < total;
+       w0 += warps * ROWS) {
+    uint4 o[UNROLL], d[UNROLL];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 a = unpack2<BF16>(ow[e]), c = unpack2<BF16>(dw[e]);
-          acc = fmaf(a.x, c.x, fmaf(a.y, c.y, acc));
+    for (int u = 0; u < UNROLL; ++u) {
+      const long long wrow = w0 + u * RPW + sub;
+      o[u] = d[u] = make_uint4(0, 0, 0, 0);
+      if (wrow < total) {
+        const long long bh = wrow / S_pad;
+        const int row = static_cast<int>(wrow % S_pad);
+        if (row < S) {
+          const int b = static_cast<int>(bh / Hq), h = static_cast<int>(bh % Hq);
+          const long long off = (static_cast<long long>(b) * o_batch_stride +
+                                 static_cast<long long>(row) * o_row_stride + static_cast<long long>(h) * D) * 2 +
+                                chunk * 16;
+          o[u] = __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(out) + off));
+          d[u] = __ldcs(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(dout) + off));
         }
       }
-#pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
     }
-    if (lane == 0) {
-      delta[wrow] = row < S ? acc : 0.f;
-      lse2[wrow] = row < S ? lse[bh * S + row] * 1.4426950408889634f : INFINITY;
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const uint32_t* ow = reinterpret_cast<const uint32_t*>(&o[u]);
+      const uint32_t* dw = reinterpret_cast<const uint32_t*>(&d[u]);
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = unpack2<BF16>(ow[e]), c = unpack2<BF16>(dw[e]);
+        acc = fmaf(a.x, c.x, fmaf(a.y, c.y, acc));
+      }
+#pragma unroll
+      for (int m = LPR / 2; m >= 1; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+      const long long wrow = w0 + u * RPW + sub;
+      if (chunk == 0 && wrow < total) {
+        const long long bh = wrow / S_pad;
+        const int row = static_cast<int>(wrow % S_pad);
+        delta[wrow] = row < S ? acc : 0.f;
+        lse2[wrow] = row < S ? lse[bh * S + row] * 1.4426950408889634f : INFINITY;
+      }
     }
   }
 }
@@ -90,7 +106,8 @@ static int grid_for(long long work, int per_block) {
 cudaError_t attn_bwd_pre(const void* out, const void* dout, const float* lse, float* lse2, float* delta,
                          long long o_row_stride, long long o_batch_stride, int B, int S, int S_pad,
                          int Hq, int D, bool bf16, cudaStream_t st) {
-  const int grid = grid_for(static_cast<long long>(B) * Hq * S_pad, 8);
+  // 8 warps per block, each covering 8 (D = 128) or 16 (D = 64) rows per pass
+  const int grid = grid_for(static_cast<long long>(B) * Hq * S_pad, 8 * (D == 64 ? 16 : 8));
 #define TKB_PRE(DD, BB) \
   attn_bwd_pre_kernel<DD, BB><<<grid, 256, 0, st>>>(out, dout, lse, lse2, delta, o_row_stride, o_batch_stride, B, S, S_pad, Hq)
   if (D == 128) { if (bf16) TKB_PRE(128, true); else TKB_PRE(128, false); }

@@ -604,11 +604,14 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
 }
 
 // ============================================================================ dQ = dS K
-// One CTA per 128-row query tile of a (batch, q head): the stored dS tiles of
-// the row (A, 128 queries x 128 keys in core-matrix order, one bulk copy
-// each) and the matching K tiles (B, TMA, 128-byte swizzle) stream through an
-// NST-stage ring; one thread issues the tcgen05 MMAs into a TMEM
-// accumulator; four warps scale and store dQ.
+// Persistent: one CTA per SM walks the (query tile, batch x q head) items in
+// longest-first order, item t of the order at CTA t mod gridDim.  For each
+// item the stored dS tiles of its query row (A, 128 queries x 128 keys in
+// core-matrix order, one bulk copy each) and the matching K tiles (B, TMA,
+// 128-byte swizzle) stream through an NST-stage ring that runs on across
+// items; one thread issues the tcgen05 MMAs into one of two TMEM
+// accumulators; four warps scale and store dQ of the previous item while the
+// next one accumulates.
 template <int D>
 struct DskCfg {
   static constexpr int SLAB = 128 * 128;
@@ -617,11 +620,25 @@ struct DskCfg {
   static constexpr int STAGE = TILE_A + TILE_K;
   static constexpr int NST = (D == 64) ? 4 : 3;
   static constexpr int OFF_BAR = NST * STAGE;
-  static constexpr int NBAR = 2 * NST + 2;      // full[NST], empty[NST], dq_done, drain
+  // full[NST], empty[NST], acc_full[2], acc_empty[2], drain
+  static constexpr int NBAR = 2 * NST + 5;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
-  static constexpr uint32_t TM_COLS = D;
+  static constexpr uint32_t TM_COLS = 2 * D;    // two accumulators
 };
+
+struct DskItem {
+  int qt, bh, nb;
+};
+
+TKB_DEVFN DskItem dsk_item(const BwdParams& p, int t) {
+  const int BH = p.B * p.Hq, nq = p.S_pad >> 7;
+  DskItem it;
+  it.qt = nq - 1 - t / BH;
+  it.bh = t % BH;
+  it.nb = p.causal ? it.qt + 1 : nq;
+  return it;
+}
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_constant__ BwdParams p) {
@@ -632,28 +649,25 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_const
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* full = bars;
   uint64_t* empty = full + C::NST;
-  uint64_t* dq_done = empty + C::NST;
-  uint64_t* mma_drain = dq_done + 1;
+  uint64_t* acc_full = empty + C::NST;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
   const int warp = warp_id(), lane = lane_id();
-  const int BH = p.B * p.Hq;
   const int nq = p.S_pad >> 7;
-  const int qt = nq - 1 - static_cast<int>(blockIdx.x / BH);  // longest (causal) first
-  const int bh = blockIdx.x % BH;
-  const int b = bh / p.Hq, h = bh % p.Hq;
-  const int g = h / (p.Hq / p.Hkv);
-  const int nb = p.causal ? qt + 1 : nq;
-  // tiles of one query row are consecutive: tile j of the row at tile0 + j
-  const long long tile0 = static_cast<long long>(bh) * p.ds_tiles + ds_tile(qt, 0, nq, p.causal);
+  const int n_items = p.B * p.Hq * nq;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(dq_done, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
     mbar_init(mma_drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -672,41 +686,58 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_const
     if (lane == 0) {
       prefetch_tmap(&p.tmK);
       const uint64_t pol_ds = policy_evict_first(), pol_k = policy_evict_last();
-      int issued = 0;
-      for (int j = 0; j < nb; ++j) {
-        const int s = j % C::NST;
-        if (!mbar_wait(&empty[s], ((j / C::NST) & 1) ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[s], C::STAGE);
-        uint8_t* st = smem + s * C::STAGE;
-        bulk_load_hint(st, reinterpret_cast<const uint8_t*>(p.ds) + (tile0 + j) * 32768, C::TILE_A, &full[s], pol_ds);
+      int n = 0;  // ring position, continuous across items
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x) {
+        const DskItem it = dsk_item(p, t);
+        const int b = it.bh / p.Hq, g = (it.bh % p.Hq) / (p.Hq / p.Hkv);
+        // the tiles of one query row are consecutive
+        const long long tile0 = static_cast<long long>(it.bh) * p.ds_tiles + ds_tile(it.qt, 0, nq, p.causal);
+        for (int j = 0; j < it.nb; ++j, ++n) {
+          const int s = n % C::NST;
+          if (!(ok = mbar_wait(&empty[s], ((n / C::NST) & 1) ^ 1, abort_flag))) break;
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          uint8_t* st = smem + s * C::STAGE;
+          bulk_load_hint(st, reinterpret_cast<const uint8_t*>(p.ds) + (tile0 + j) * 32768, C::TILE_A, &full[s],
+                         pol_ds);
 #pragma unroll
-        for (int hh = 0; hh < D / 64; ++hh)
-          tma_load_3d(st + C::TILE_A + hh * C::SLAB, &p.tmK, &full[s], g * D + hh * 64, j * 128, b, pol_k);
-        issued = j + 1;
+          for (int hh = 0; hh < D / 64; ++hh)
+            tma_load_3d(st + C::TILE_A + hh * C::SLAB, &p.tmK, &full[s], g * D + hh * 64, j * 128, b, pol_k);
+        }
       }
-      if (*abort_flag) {
+      if (!ok) {
+        // let the copies in flight land before the CTA exits
         volatile int never = 0;
-        for (int j = max(0, issued - C::NST); j < issued; ++j) mbar_wait(&full[j % C::NST], (j / C::NST) & 1, &never);
+        for (int m = max(0, n - C::NST); m < n; ++m) mbar_wait(&full[m % C::NST], (m / C::NST) & 1, &never);
       }
     }
   } else if (warp == 5) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t id = idesc_f16kind(128, D, BF16, true, true);  // A query-major, B key-major
+      int n = 0, k = 0;  // ring position; item count of this CTA
       bool ok = true;
-      for (int j = 0; j < nb; ++j) {
-        const int s = j % C::NST;
-        if (!(ok = mbar_wait(&full[s], (j / C::NST) & 1, abort_flag))) break;
+      for (int t = blockIdx.x; ok && t < n_items; t += gridDim.x, ++k) {
+        const DskItem it = dsk_item(p, t);
+        const int a = k & 1;
+        // the epilogue has emptied this accumulator (item k - 2)
+        if (!(ok = mbar_wait(&acc_empty[a], ((k >> 1) & 1) ^ 1, abort_flag))) break;
         tc_fence_after();
-        const uint32_t sa = sbase + s * C::STAGE, sk = sa + C::TILE_A;
+        const uint32_t acc = tmem + a * D;
+        for (int j = 0; j < it.nb; ++j, ++n) {
+          const int s = n % C::NST;
+          if (!(ok = mbar_wait(&full[s], (n / C::NST) & 1, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t sa = sbase + s * C::STAGE, sk = sa + C::TILE_A;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem, sdesc_interleave(sa + kk * 4096, 2048, 128), sdesc_sw128(sk + kk * 2048, C::SLAB, 1024), id,
-                  (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&empty[s]);
+          for (int kk = 0; kk < 8; ++kk)
+            umma_ss(acc, sdesc_interleave(sa + kk * 4096, 2048, 128), sdesc_sw128(sk + kk * 2048, C::SLAB, 1024), id,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[a]);
       }
-      if (ok) umma_commit(dq_done);
-      else {
+      if (!ok) {
         volatile int never = 0;
         umma_commit(mma_drain);
         mbar_wait(mma_drain, 0, &never);
@@ -715,17 +746,22 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_const
   } else {
     // ---------------------------------------------------------------- epilogue: warps 0-3, one query row each
     const int r = threadIdx.x;  // TMEM lane
-    const int qrow = qt * 128 + r;
     const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    if (nb > 0 && mbar_wait(dq_done, 0, abort_flag)) {
+    int k = 0;
+    for (int t = blockIdx.x; t < n_items; t += gridDim.x, ++k) {
+      const DskItem it = dsk_item(p, t);
+      const int a = k & 1;
+      if (!mbar_wait(&acc_full[a], (k >> 1) & 1, abort_flag)) break;
       tc_fence_after();
+      const int b = it.bh / p.Hq, h = it.bh % p.Hq;
+      const int qrow = it.qt * 128 + r;
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.dq) +
                      2 * (static_cast<long long>(b) * p.dkv_batch_stride +
                           static_cast<long long>(qrow) * p.dkv_row_stride + static_cast<long long>(h) * D);
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t v[32];
-        tmem_ld32(tmem + lane_off + c * 32, v);
+        tmem_ld32(tmem + lane_off + a * D + c * 32, v);
         wait_ld_dep32(v);
         uint4 o[4];
         uint32_t* ow = reinterpret_cast<uint32_t*>(o);
@@ -738,6 +774,8 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_const
           for (int e = 0; e < 4; ++e) d4[e] = o[e];
         }
       }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
     }
   }
 
@@ -764,7 +802,11 @@ static cudaError_t launch_bwd(const BwdParams& p, cudaStream_t stream) {
     auto kern = attn_bwd_dsk_kernel<D, BF16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
-    kern<<<static_cast<unsigned>(p.B * p.Hq * (p.S_pad / 128)), 192, C::SMEM, stream>>>(p);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int items = p.B * p.Hq * (p.S_pad / 128);
+    kern<<<static_cast<unsigned>(items < sms ? items : sms), 192, C::SMEM, stream>>>(p);
     return cudaGetLastError();
   }
   {
