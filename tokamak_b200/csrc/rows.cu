@@ -706,12 +706,15 @@ __global__ void __launch_bounds__(NTH) softmax_loss_kernel(const T* __restrict__
 
 // Streaming variant for wide rows (vocabularies): two passes over the row
 // instead of holding it in registers, so a 256-thread block per row keeps
-// its registers low and eight rows in flight per SM.  Pass 1 keeps per-thread
-// online statistics (running max m, s1 = sum e^(x-m), s2 = sum e^(2(x-m)) for
-// the Brier score, first-index argmax, the label logit); pass 2 re-reads the
-// row (mostly from L2) and writes the gradient.  Same results as
-// softmax_loss_kernel (src/tkm_gpu.cu:632-682).
-template <typename T, int VEC>
+// its registers low.  Pass 1 keeps per-thread online statistics (running max
+// m, s1 = sum e^(x-m), s2 = sum e^(2(x-m)) for the Brier score, first-index
+// argmax, the label logit); pass 2 reads the row again and writes the
+// gradient.  STAGE: the row is first brought into shared memory by one bulk
+// copy (rows of at most 72 KB, three blocks per SM), so that HBM sees one read
+// of the logits and both passes read shared memory; otherwise pass 2 re-reads
+// global memory (mostly L2) with eight rows in flight per SM.  Same results
+// as softmax_loss_kernel (src/tkm_gpu.cu:632-682).
+template <typename T, int VEC, bool STAGE>
 __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __restrict__ logits,
                                                                   const int32_t* __restrict__ labels,
                                                                   T* __restrict__ dlogits, float* __restrict__ row_loss,
@@ -720,17 +723,42 @@ __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __res
   constexpr int NTH = 256;
   __shared__ float shm[NTH / 32], sh1[NTH / 32], sh2[NTH / 32], shx[NTH / 32];
   __shared__ int sha[NTH / 32];
+  __shared__ uint64_t row_full;
+  __shared__ int abort_flag;
+  extern __shared__ __align__(16) uint8_t stage_raw[];
+  T* stage = reinterpret_cast<T*>(stage_raw);
+  const uint32_t row_bytes = static_cast<uint32_t>(C) * sizeof(T);
   const int nvec = C / VEC;
   const float inv_rows = 1.0f / static_cast<float>(rows);
   const bool brier = kind == 2;
-  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
+  if constexpr (STAGE) {
+    if (threadIdx.x == 0) {
+      mbar_init(&row_full, 1);
+      abort_flag = 0;
+      fence_barrier_init();
+    }
+    __syncthreads();
+  }
+  int it = 0;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
     const long long base = static_cast<long long>(row) * C;
     const int y = labels ? labels[row] : 0;
+    const T* src = logits + base;
+    if constexpr (STAGE) {
+      if (threadIdx.x == 0) {
+        // the previous row's reads of the buffer (generic proxy) come first
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&row_full, row_bytes);
+        bulk_load(stage, logits + base, row_bytes, &row_full);
+      }
+      if (!mbar_wait(&row_full, it & 1, &abort_flag)) return;  // bounded; error word set
+      src = stage;
+    }
     float m = -INFINITY, s1 = 0.f, s2 = 0.f, xy = 0.f, best = -INFINITY;
     int arg = 0x7fffffff;
     for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
       float v[VEC];
-      ldv<T, VEC>(logits + base + static_cast<long long>(vi) * VEC, v);
+      ldv<T, VEC>(src + static_cast<long long>(vi) * VEC, v);
       float vm = v[0];
       int va = 0;
 #pragma unroll
@@ -743,16 +771,28 @@ __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __res
           if (vi * VEC + e == y) xy = v[e];
       }
       if (vm > m) {
-        const float r = exp2f((m - vm) * 1.4426950408889634f);
+        const float r = ex2((m - vm) * 1.4426950408889634f);
         s1 *= r;
         s2 *= r * r;
         m = vm;
       }
+      // e^(x - m) = 2^(x log2 e - m log2 e): one FMA and one MUFU ex2 each
+      const float nml = -m * 1.4426950408889634f;
+      if (brier) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const float ex = exp2f((v[e] - m) * 1.4426950408889634f);
-        s1 += ex;
-        if (brier) s2 = fmaf(ex, ex, s2);
+        for (int e = 0; e < VEC; ++e) {
+          const float ex = ex2(fmaf(v[e], 1.4426950408889634f, nml));
+          s1 += ex;
+          s2 = fmaf(ex, ex, s2);
+        }
+      } else {
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; e += 2) {
+          a0 += ex2(fmaf(v[e], 1.4426950408889634f, nml));
+          a1 += ex2(fmaf(v[e + 1], 1.4426950408889634f, nml));
+        }
+        s1 += a0 + a1;
       }
     }
     // combine the threads' (m, s1, s2), argmax (first index on ties) and label logit
@@ -816,22 +856,34 @@ __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __res
       if (correct && A == y) atomicAdd(correct, 1);
     }
     if (dlogits) {
+      // gradient / rows = pc * (ga + gb * pc), minus gsub at the label:
+      //   CE    pc - t                 -> ga = 1,          gb = 0,  gsub = 1
+      //   focal fgs (pc - t)           -> ga = fgs,        gb = 0,  gsub = fgs
+      //   Brier k2 pc ((pc - t) - bdot) -> ga = -k2 bdot,  gb = k2, gsub = k2 pc
       const float k2 = 2.0f / static_cast<float>(C);
+      const float ga = (kind == 0 ? 1.f : kind == 1 ? fgs : -k2 * bdot) * inv_rows;
+      const float gb = (kind == 2 ? k2 : 0.f) * inv_rows;
+      const float nml = -M * 1.4426950408889634f, es = inv_s;
       for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
         float v[VEC], o[VEC];
-        ldv<T, VEC>(logits + base + static_cast<long long>(vi) * VEC, v);
+        ldv<T, VEC>(src + static_cast<long long>(vi) * VEC, v);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
-          const float pc = exp2f((v[e] - M) * 1.4426950408889634f) * inv_s, t = (vi * VEC + e == y) ? 1.f : 0.f;
-          float gr;
-          if (kind == 0) gr = pc - t;
-          else if (kind == 1) gr = fgs * (pc - t);
-          else gr = k2 * pc * ((pc - t) - bdot);
-          o[e] = gr * inv_rows;
+          const float pc = ex2(fmaf(v[e], 1.4426950408889634f, nml)) * es;
+          o[e] = pc * fmaf(gb, pc, ga);
+        }
+        if (y >= vi * VEC && y < vi * VEC + VEC) {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e)
+            if (vi * VEC + e == y) {
+              const float pc = ex2(fmaf(v[e], 1.4426950408889634f, nml)) * es;
+              o[e] -= (kind == 0 ? 1.f : kind == 1 ? fgs : k2 * pc) * inv_rows;
+            }
         }
         stv<T, VEC>(dlogits + base + static_cast<long long>(vi) * VEC, o);
       }
     }
+    if constexpr (STAGE) __syncthreads();  // every read of the buffer is done before the next copy
   }
 }
 
@@ -1123,9 +1175,16 @@ static cudaError_t softmax_bwd_t(const void* p, const void* dp, void* dx, int ro
 template <typename T>
 static cudaError_t softmax_loss_t(const void* logits, const int32_t* labels, void* dlogits, float* loss, int* correct,
                                   float* row_loss, int rows, int C, int kind, float gamma, cudaStream_t st) {
-  if (C % 8 == 0 && C >= 8192)
-    softmax_loss_stream_kernel<T, 8><<<row_grid(rows, 8), 256, 0, st>>>((const T*)logits, labels, (T*)dlogits,
-                                                                        row_loss, correct, rows, C, kind, gamma);
+  const size_t row_bytes = static_cast<size_t>(C) * sizeof(T);
+  if (C % 8 == 0 && C >= 8192 && row_bytes <= 72 * 1024) {
+    auto kern = softmax_loss_stream_kernel<T, 8, true>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(row_bytes));
+    if (e != cudaSuccess) return e;
+    kern<<<row_grid(rows, 3), 256, row_bytes, st>>>((const T*)logits, labels, (T*)dlogits, row_loss, correct, rows, C,
+                                                    kind, gamma);
+  } else if (C % 8 == 0 && C >= 8192)
+    softmax_loss_stream_kernel<T, 8, false><<<row_grid(rows, 8), 256, 0, st>>>((const T*)logits, labels, (T*)dlogits,
+                                                                               row_loss, correct, rows, C, kind, gamma);
   else if (C % 8 == 0)
     TKB_WIDE_DISPATCH(softmax_loss_kernel, T, 8, C, rows, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
                       rows, C, kind, gamma);
