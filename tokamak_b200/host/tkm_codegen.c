@@ -115,6 +115,10 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
     o->rpb = o->tpr >= 256 ? 1 : 256 / o->tpr;
     o->threads = o->tpr * o->rpb;
     o->fwd_grid = (o->rows + o->rpb - 1) / o->rpb;
+    /* measured: prefetching the next row pays for elementwise groups (twin
+     * 0.69 -> 0.76, bias 0.82 -> 0.91 of HBM) but costs a normalisation the
+     * resident blocks that its row reduction needs (0.65 -> 0.60) */
+    o->persist = !group_has_norm(g, pg);
 }
 
 void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *o) {
@@ -471,14 +475,20 @@ static void copy_array(Buf *b, const char *dst, const char *src) {
             dst, src);
 }
 
-static void load_array(Buf *b, const char *arr, const char *src, const char *row_pairs, const char *col0) {
-    decl_array(b, arr);
+/* loads `arr` (declared by the caller) from row `rowv` when `okv` holds */
+static void load_into(Buf *b, const char *arr, const char *src, const char *row_pairs, const char *col0,
+                      const char *rowv, const char *okv) {
     bprintf(b,
             "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\n"
             "    const int tkm_ch = tkm_lr + k * TKG_TPR;\n"
-            "    if (tkm_row_ok && tkm_ch < TKG_NCH) tkm_ld<TKG_VP>(%s, (long long)row * %s + %s + tkm_ch * TKG_VP, %s[k]);\n"
+            "    if (%s && tkm_ch < TKG_NCH) tkm_ld<TKG_VP>(%s, (long long)%s * %s + %s + tkm_ch * TKG_VP, %s[k]);\n"
             "    else tkm_zero<TKG_VP>(%s[k]);\n  }\n",
-            src, row_pairs, col0, arr, arr);
+            okv, src, rowv, row_pairs, col0, arr, arr);
+}
+
+static void load_array(Buf *b, const char *arr, const char *src, const char *row_pairs, const char *col0) {
+    decl_array(b, arr);
+    load_into(b, arr, src, row_pairs, col0, "row", "tkm_row_ok");
 }
 
 static void store_array(Buf *b, const char *dst, const char *row_pairs, const char *col0, const char *arr, int acc) {
@@ -774,7 +784,95 @@ static void emit_branch_loads(Em *e, int skip) {
     }
 }
 
+/* inputs of one forward row: (array, source, row stride in pairs, column offset) */
+typedef struct {
+    char arr[16];
+    const char *src;
+    const char *stride;
+    const char *col0;
+} FwdInput;
+
+static int fwd_inputs(Em *e, FwdInput *in) {
+    int n = 0;
+    const char *a = A(e, KA_IN, -1, 0);
+    if (e->pg->is_twin_epilogue) {
+        in[n++] = (FwdInput){"txl", a, "(2 * TKG_C2)", "0"};
+        in[n++] = (FwdInput){"txr", a, "(2 * TKG_C2)", "TKG_C2"};
+    } else {
+        in[n++] = (FwdInput){"tx", a, "TKG_C2", "0"};
+    }
+    for (int i = 0; i < e->L.n && n < 16; i++) {
+        const TkmNode *nd = &e->g->nodes[e->L.ids[i]];
+        if (nd->op != OP_ADD) continue;
+        FwdInput f = {"", A(e, KA_BRANCH, nd->id, 0), "TKG_C2", "0"};
+        snprintf(f.arr, sizeof(f.arr), "tbr_%d", i);
+        in[n++] = f;
+    }
+    return n;
+}
+
+/* The forward is persistent: each block walks row blocks tkm_rb, blockIdx.x +
+ * k gridDim.x, with the next row block's inputs requested before the current
+ * one is computed, and loads its per-channel parameters once. */
+static void emit_plasma_fwd_rowblock(Em *e);
+
 static void emit_plasma_fwd(Em *e) {
+    TkmRowGeom gm;
+    tkm_row_geom(e->g, e->pg, 2, &gm);
+    if (!gm.persist) {
+        emit_plasma_fwd_rowblock(e);
+        return;
+    }
+    Buf *b = e->b;
+    const Lists *L = &e->L;
+    set_args(e, 0);
+    e->acc_smem = 0;
+    e->param_regs = 1;
+    kernel_head(e, "fwd", 0);
+    if (range_has_norm(e, 0, L->n)) bprintf(b, "  __shared__ float tkm_red[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
+    emit_param_preload(e);
+    FwdInput in[16];
+    const int nin = fwd_inputs(e, in);
+    char nx[24];
+    bprintf(b, "  int tkm_rb = blockIdx.x;\n"
+               "  {\n    const int rown = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "    const bool okn = tkm_rb < TKG_NRB && rown < TKG_ROWS;\n");
+    for (int i = 0; i < nin; i++) {
+        snprintf(nx, sizeof(nx), "%s_nx", in[i].arr);
+        bprintf(b, "  float2 %s[TKG_KCH][TKG_VP];\n", nx);
+        load_into(b, nx, in[i].src, in[i].stride, in[i].col0, "rown", "okn");
+    }
+    bprintf(b, "  for (; tkm_rb < TKG_NRB; tkm_rb += gridDim.x) {\n"
+               "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "  const bool tkm_row_ok = row < TKG_ROWS;\n");
+    for (int i = 0; i < nin; i++) {
+        snprintf(nx, sizeof(nx), "%s_nx", in[i].arr);
+        decl_array(b, in[i].arr);
+        copy_array(b, in[i].arr, nx);
+    }
+    bprintf(b, "  {\n    const int rbn = tkm_rb + gridDim.x;\n"
+               "    const int rown = rbn * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "    const bool okn = rbn < TKG_NRB && rown < TKG_ROWS;\n");
+    for (int i = 0; i < nin; i++) {
+        snprintf(nx, sizeof(nx), "%s_nx", in[i].arr);
+        load_into(b, nx, in[i].src, in[i].stride, in[i].col0, "rown", "okn");
+    }
+    bprintf(b, "  }\n");
+    declare_stats(e);
+    if (e->pg->is_twin_epilogue) {
+        for (int i = 0; i < L->nl; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txl", 0);
+        for (int i = L->nl; i < L->nl + L->nr; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txr", 0);
+        decl_array(b, "tx");
+        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
+                   "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
+    }
+    for (int i = L->nl + L->nr; i < L->n; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "tx", 0);
+    store_array(b, A(e, KA_OUT, -1, 0), "TKG_C2", "0", "tx", 0);
+    bprintf(b, "  }\n  }\n}\n\n");
+}
+
+/* one row block per block (normalisation groups) */
+static void emit_plasma_fwd_rowblock(Em *e) {
     Buf *b = e->b;
     const Lists *L = &e->L;
     set_args(e, 0);

@@ -62,6 +62,8 @@ typedef struct {
     int ncb;     /* column blocks: > 1 splits a row over blockIdx.y (no row statistics) */
     int rows;    /* batch_size * H * W */
     int fwd_grid;
+    int persist; /* forward kernel loops over row blocks with the next one prefetched
+                  * (groups without a normalisation); else one row block per block */
 } TkmRowGeom;
 
 void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *geom);
