@@ -156,6 +156,51 @@ static void group_lists(const TkmGraph *g, const PlasmaGroup *pg, Lists *L) {
     L->nc = L->n - L->nl - L->nr;
 }
 
+/* Rows a backward kernel stages (tkm_group_bwd_stage_bytes): the group input
+ * (both halves for a twin epilogue), dout, and the second input of every Add
+ * but a trailing one (whose forward the backward does not replay). */
+static int bwd_needs_input(const TkmGraph *g, const PlasmaGroup *pg);
+
+static int bwd_staged_rows(const TkmGraph *g, const PlasmaGroup *pg) {
+    Lists L;
+    group_lists(g, pg, &L);
+    if (!pg->is_twin_epilogue && !bwd_needs_input(g, pg)) return 1; /* dout only */
+    int n = (pg->is_twin_epilogue ? 2 : 1) + 1;
+    const int last = L.n - 1;
+    const int skip = (L.nc > 0 && g->nodes[L.ids[last]].cat != CAT_NORM) ? last : -1;
+    for (int i = 0; i < L.n; i++)
+        if (g->nodes[L.ids[i]].op == OP_ADD && i != skip) n++;
+    return n;
+}
+
+/* A chain of Bias and Add operators only (outside a twin epilogue) has a
+ * backward that needs dout alone: its input is neither loaded nor replayed. */
+static int bwd_needs_input(const TkmGraph *g, const PlasmaGroup *pg) {
+    if (pg->is_twin_epilogue) return 1;
+    Lists L;
+    group_lists(g, pg, &L);
+    for (int i = L.nl + L.nr; i < L.n; i++) {
+        const int op = g->nodes[L.ids[i]].op;
+        if (op != OP_BIAS && op != OP_ADD) return 1;
+    }
+    return 0;
+}
+
+int tkm_group_bwd_row_inputs(const TkmGraph *g, const PlasmaGroup *pg) { return bwd_staged_rows(g, pg); }
+
+/* measured: staging pays for backward kernels that read several rows per row
+ * (twin 0.78 -> 0.82 of HBM, norm 166 -> 163 us); one that streams dout alone
+ * runs faster on plain loads (182 vs 210 us) */
+int tkm_group_bwd_stage_bytes(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes) {
+    if (pg->is_qkv_prep) return 0;
+    const int nrows = bwd_staged_rows(g, pg);
+    if (nrows < 2) return 0;
+    TkmRowGeom gm;
+    tkm_row_geom_bwd(g, pg, act_bytes, &gm);
+    const long bytes = 2L * nrows * gm.kch * gm.threads * 16;
+    return bytes <= 128 * 1024 ? (int)bytes : 0;
+}
+
 static uint32_t node_flags(const TkmGraph *g, int id) {
     const TkmOpSpec *sp = tkm_find_spec_by_node(&g->nodes[id]);
     return sp ? sp->res_flags : 0;
@@ -710,8 +755,9 @@ static void emit_geom_macros(Em *e, int bwd) {
         const TkmRowGeom *gm = gs[i];
         bprintf(b, i == 0 ? "#if TKM_ACT_BYTES == 2\n" : "#else\n");
         bprintf(b, "#define TKG_VP %d\n#define TKG_NCH %d\n#define TKG_TPR %d\n#define TKG_KCH %d\n#define TKG_RPB %d\n"
-                   "#define TKG_THREADS %d\n#define TKG_CB %d\n",
-                gm->vp, gm->nch, gm->tpr, gm->kch, gm->rpb, gm->threads, gm->ncb);
+                   "#define TKG_THREADS %d\n#define TKG_CB %d\n#define TKG_STAGE_BYTES %d\n",
+                gm->vp, gm->nch, gm->tpr, gm->kch, gm->rpb, gm->threads, gm->ncb,
+                bwd ? tkm_group_bwd_stage_bytes(e->g, e->pg, i == 0 ? 2 : 4) : 0);
     }
     bprintf(b, "#endif\n#define TKG_C2 %d\n#define TKG_ROWS %d\n#define TKG_INV_C ", g2.C2, g2.rows);
     emit_float(b, 1.0 / (double)g2.C);
@@ -720,6 +766,7 @@ static void emit_geom_macros(Em *e, int bwd) {
 
 static void undef_geom(Buf *b) {
     bprintf(b, "#undef TKG_VP\n#undef TKG_NCH\n#undef TKG_TPR\n#undef TKG_KCH\n#undef TKG_RPB\n#undef TKG_THREADS\n#undef TKG_CB\n"
+               "#undef TKG_STAGE_BYTES\n"
                "#undef TKG_C2\n#undef TKG_ROWS\n#undef TKG_INV_C\n#undef TKG_NRB\n");
 }
 
@@ -985,6 +1032,25 @@ static void emit_partials(Em *e, int qkv) {
     }
 }
 
+
+/* cp.async of every input chunk of row block `rbn` (a variable of the
+ * emitted code) into stage slot `slot_fmt` (a printf format with one int, or
+ * a variable name when slot_val < 0) */
+static void emit_stage_issue(Em *e, const FwdInput *rin, int nin, const char *slot_fmt, int slot_val) {
+    Buf *b = e->b;
+    char slot[24];
+    if (slot_val >= 0) snprintf(slot, sizeof(slot), slot_fmt, slot_val);
+    else snprintf(slot, sizeof(slot), "%s", slot_fmt);
+    bprintf(b, "    const int rown = rbn * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "    const bool okn = rbn < TKG_NRB && rown < TKG_ROWS;\n");
+    for (int i = 0; i < nin; i++)
+        bprintf(b, "    _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\n"
+                   "      const int tkm_ch = tkm_lr + k * TKG_TPR;\n"
+                   "      tkm_cp<TKG_VP>(&TKM_STG(%s, %d, k), %s, (long long)rown * %s + %s + tkm_ch * TKG_VP,\n"
+                   "                     okn && tkm_ch < TKG_NCH);\n    }\n",
+                slot, i, rin[i].src, rin[i].stride, rin[i].col0);
+}
+
 static void emit_plasma_bwd(Em *e) {
     Buf *b = e->b;
     const Lists *L = &e->L;
@@ -1002,30 +1068,64 @@ static void emit_plasma_bwd(Em *e) {
                    "  __shared__ float2 tkm_red2[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
     declare_accs(e);
     if (e->param_regs) emit_param_preload(e);
-    bprintf(b, "  for (int tkm_rb = blockIdx.x; tkm_rb < TKG_NRB; tkm_rb += gridDim.x) {\n"
-               "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
-               "  const bool tkm_row_ok = row < TKG_ROWS;\n");
-    declare_stats(e);
     const char *in = A(e, KA_IN, -1, 0);
     /* every input of the row is requested before any row statistics */
     const int last = L->n - 1;
     const int skip = (L->nc > 0 && e->g->nodes[L->ids[last]].cat != CAT_NORM) ? last : -1;
+    FwdInput rin[16];
+    int nin = 0;
+    const int need_x = bwd_needs_input(e->g, e->pg);
     if (e->pg->is_twin_epilogue) {
-        load_array(b, "txl", in, "(2 * TKG_C2)", "0");
-        load_array(b, "txr", in, "(2 * TKG_C2)", "TKG_C2");
-        load_array(b, "tg", A(e, KA_DOUT, -1, 0), "TKG_C2", "0");
-        emit_branch_loads(e, skip);
+        rin[nin++] = (FwdInput){"txl", in, "(2 * TKG_C2)", "0"};
+        rin[nin++] = (FwdInput){"txr", in, "(2 * TKG_C2)", "TKG_C2"};
+    } else if (need_x) {
+        rin[nin++] = (FwdInput){"tx", in, "TKG_C2", "0"};
+    }
+    rin[nin++] = (FwdInput){"tg", A(e, KA_DOUT, -1, 0), "TKG_C2", "0"};
+    for (int i = 0; i < L->n && nin < 16 && need_x; i++) {
+        const TkmNode *nd = &e->g->nodes[L->ids[i]];
+        if (nd->op != OP_ADD || i == skip) continue;
+        FwdInput f = {"", A(e, KA_BRANCH, nd->id, 0), "TKG_C2", "0"};
+        snprintf(f.arr, sizeof(f.arr), "tbr_%d", i);
+        rin[nin++] = f;
+    }
+    /* TKG_STAGE_BYTES > 0 (per storage type, tkm_group_bwd_stage_bytes):
+     * rows are staged two row blocks ahead by cp.async into dynamic
+     * shared-memory slots private to each thread, so that their loads are in
+     * flight while the current row computes, without holding registers. */
+    bprintf(b, "#if TKG_STAGE_BYTES > 0\n"
+               "  extern __shared__ uint4 tkm_dyn[];\n"
+               "#define TKM_STG(s, a, k) tkm_dyn[(((s) * %d + (a)) * TKG_KCH + (k)) * TKG_THREADS + threadIdx.x]\n",
+            nin);
+    for (int ahead = 0; ahead < 2; ahead++) {
+        bprintf(b, "  {\n    const int rbn = blockIdx.x + %d * gridDim.x;\n", ahead);
+        emit_stage_issue(e, rin, nin, "%d", ahead);
+        bprintf(b, "  }\n  tkm_cp_commit();\n");
+    }
+    bprintf(b, "#endif\n  int tkm_it = 0; (void)tkm_it;\n");
+    bprintf(b, "  for (int tkm_rb = blockIdx.x; tkm_rb < TKG_NRB; tkm_rb += gridDim.x, ++tkm_it) {\n"
+               "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "  const bool tkm_row_ok = row < TKG_ROWS;\n");
+    declare_stats(e);
+    bprintf(b, "#if TKG_STAGE_BYTES > 0\n  const int tkm_sl = tkm_it & 1;\n  tkm_cp_wait<1>();\n");
+    for (int i = 0; i < nin; i++) {
+        decl_array(b, rin[i].arr);
+        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) tkm_lds<TKG_VP>(&TKM_STG(tkm_sl, %d, k), %s[k]);\n",
+                i, rin[i].arr);
+    }
+    bprintf(b, "  {\n    const int rbn = tkm_rb + 2 * gridDim.x;\n");
+    emit_stage_issue(e, rin, nin, "tkm_sl", -1);
+    bprintf(b, "  }\n  tkm_cp_commit();\n#else\n");
+    for (int i = 0; i < nin; i++) load_array(b, rin[i].arr, rin[i].src, rin[i].stride, rin[i].col0);
+    bprintf(b, "#endif\n");
+    if (e->pg->is_twin_epilogue) {
         emit_replay(e, 0, L->nl, "txl", 0);
         emit_replay(e, L->nl, L->nl + L->nr, "txr", 0);
         decl_array(b, "tx");
         bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
                    "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
-    } else {
-        load_array(b, "tx", in, "TKG_C2", "0");
-        load_array(b, "tg", A(e, KA_DOUT, -1, 0), "TKG_C2", "0");
-        emit_branch_loads(e, skip);
     }
-    emit_replay(e, L->nl + L->nr, L->n, "tx", 1);
+    if (need_x) emit_replay(e, L->nl + L->nr, L->n, "tx", 1);
     emit_bwd_range(e, L->nl + L->nr, L->n, "tg");
     const char *din = A(e, KA_DIN, -1, 0);
     if (e->pg->is_twin_epilogue) {
@@ -1042,6 +1142,8 @@ static void emit_plasma_bwd(Em *e) {
         store_array(b, din, "TKG_C2", "0", "tg", din_acc);
     }
     bprintf(b, "  }\n");
+    bprintf(b, "#if TKG_STAGE_BYTES > 0\n  tkm_cp_wait<0>();  /* no copy into shared memory outlives the block */\n"
+               "#undef TKM_STG\n#endif\n");
     emit_partials(e, 0);
     bprintf(b, "}\n#undef TKM_ACC\n\n");
 }

@@ -71,6 +71,12 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
  * keep more state per chunk in the backward) */
 void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *geom);
 int tkm_sm_count_hint(void);
+/* dynamic shared memory of a plasma backward kernel: its two stages of row
+ * inputs (0: the kernel loads rows directly) */
+int tkm_group_bwd_stage_bytes(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes);
+/* row-sized inputs a plasma backward kernel reads (dout, the group input and
+ * replayed Add branches when its backward needs them; a twin input counts 2) */
+int tkm_group_bwd_row_inputs(const TkmGraph *g, const PlasmaGroup *pg);
 
 /* ------------------------------------------------ plasma kernel arguments
  * Argument list of a generated kernel (forward or backward).  The code

@@ -102,6 +102,38 @@ __device__ __forceinline__ void tkm_st_add(tkm_act_t* base, long long p, const f
   tkm_st<VP>(base, p, o);
 }
 
+// ----------------------------------------------------------- async row staging
+// cp.async of one chunk (VP channel pairs) of a row into a shared-memory slot
+// private to the thread; !ok fills the slot with zeros (no global read).
+template <int VP>
+__device__ __forceinline__ void tkm_cp(void* slot, const tkm_act_t* base, long long p, bool ok) {
+  constexpr int BYTES = VP * 2 * TKM_ACT_BYTES;
+  const tkm_act_t* src = ok ? base + 2 * p : base;
+  const unsigned dst = static_cast<unsigned>(__cvta_generic_to_shared(slot));
+  const int n = ok ? BYTES : 0;
+  if constexpr (BYTES == 16)  // streamed once: not kept in L1
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(dst), "l"(src), "n"(BYTES), "r"(n) : "memory");
+}
+__device__ __forceinline__ void tkm_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void tkm_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// a staged chunk back from the thread's slot
+template <int VP>
+__device__ __forceinline__ void tkm_lds(const void* slot, float2 (&v)[VP]) {
+#if TKM_ACT_BYTES == 2
+  const uint32_t* w = reinterpret_cast<const uint32_t*>(slot);
+#pragma unroll
+  for (int i = 0; i < VP; ++i) v[i] = tkm_bf16x2_to_f2(w[i]);
+#else
+  const float2* f = reinterpret_cast<const float2*>(slot);
+#pragma unroll
+  for (int i = 0; i < VP; ++i) v[i] = f[i];
+#endif
+}
+
 // ----------------------------------------------------------- reductions
 // Rows occupy TPR consecutive threads (TPR a power of two <= 32, or a
 // multiple of 32); every thread of the block calls these.
