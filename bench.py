@@ -61,6 +61,15 @@ def load_traffic():
     return {}
 
 
+def load_rows_traffic():
+    """DRAM bytes per launch of the generated row kernels (one ncu capture)."""
+    p = os.path.join(ROOT, "profiles", "rows_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get("bytes_per_launch", {})
+    return {}
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled during the timed region."""
 
@@ -577,7 +586,7 @@ flow:
             "kernels": rows,
             "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": dom["GB/s"], "peak": hbm, "unit": "GB/s",
                          "frac": dom["GB/s"] / hbm, "peak_source": f"{src} HBM copy (MEASURED_PEAKS.json)",
-                         "traffic": None},
+                         "traffic": load_rows_traffic().get(dom["name"])},
             "e2e": None, "cpu_baseline": None, "gpu_launches": len(rows)}))
     dist_done(world)
     return 0
