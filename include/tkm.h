@@ -267,6 +267,14 @@ TKM_API int tkm_runtime_param_count(const TkmRuntime *rt);
 /* Last error message of the runtime (empty when none). */
 TKM_API const char *tkm_last_error(void);
 
+/* SGD momentum state, beside the TKM1 weight checkpoint: magic "TKMV", tensor
+ * count, then per tensor (TKM1 order) its value count and fp32 velocities; a
+ * tensor the step does not update (dead node) has 0 values.  Saving both and
+ * loading both resumes training exactly where it stopped. */
+TKM_API size_t tkm_runtime_optimizer_bytes(const TkmRuntime *rt);
+TKM_API int tkm_save_optimizer_buffer(TkmRuntime *rt, void *buffer, size_t capacity, size_t *out_size);
+TKM_API int tkm_load_optimizer_buffer(TkmRuntime *rt, const void *buffer, size_t size);
+
 /* Data-parallel training over NCCL: rank 0 creates a 128-byte NCCL unique id,
  * the caller sends it to every rank (any transport), then each rank calls
  * tkm_runtime_init_dp before its first step.  Every step then averages the

@@ -273,6 +273,37 @@ def test_weights_roundtrip_forward_and_eval():
     inf.close()
 
 
+def test_optimizer_state_resumes_training_exactly():
+    """TKM1 weights + TKMV momentum saved after some steps and loaded into a
+    fresh runtime continue bit-identically; weights alone lose the momentum."""
+    rt_mod = runtime_mod()
+    dsl = "input: 1x1x64\nflow:\n  m: FC(128) -> RMSNorm -> SiLU -> FC(10) -> SoftmaxCE\n"
+    rng = np.random.default_rng(5)
+    a = rt_mod.Runtime.from_dsl(dsl, 16, rt_mod.DTYPE_F32)
+    x = rng.normal(0, 1, a.input_elements).astype(np.float32)
+    y = rng.integers(0, 10, 16).astype(np.uint8)
+    for _ in range(3):
+        a.step(x, y, 0.05)
+    w, v = a.save_weights(), a.save_optimizer()
+    head = np.frombuffer(v[:8], dtype=np.uint32)
+    assert head[0] == 0x544B4D56 and head[1] == np.frombuffer(w[4:8], dtype=np.uint32)[0]
+    loss_a = a.step(x, y, 0.05)
+    w_a = a.save_weights()
+    b = rt_mod.Runtime.from_dsl(dsl, 16, rt_mod.DTYPE_F32)
+    b.load_weights(w)
+    b.load_optimizer(v)
+    assert b.step(x, y, 0.05) == loss_a
+    assert b.save_weights() == w_a
+    c = rt_mod.Runtime.from_dsl(dsl, 16, rt_mod.DTYPE_F32)
+    c.load_weights(w)
+    c.step(x, y, 0.05)
+    assert c.save_weights() != w_a  # momentum matters
+    with pytest.raises(rt_mod.TkbError):
+        c.load_optimizer(v[:-4])  # truncated state is rejected
+    for r in (a, b, c):
+        r.close()
+
+
 def test_training_reduces_loss_and_is_deterministic():
     rt_mod = runtime_mod()
     from tokamak_b200.configs import C1, dsl_for

@@ -50,6 +50,9 @@ _SIGS = {
     "tkm_runtime_profile": ([_vp, _i, _vp, _i], _i),
     "tkm_runtime_init_weights": ([_vp, _c.c_ulonglong, _f], _i),
     "tkm_runtime_stream": ([_vp], _vp),
+    "tkm_runtime_optimizer_bytes": ([_vp], _sz),
+    "tkm_save_optimizer_buffer": ([_vp, _vp, _sz, _c.POINTER(_sz)], _i),
+    "tkm_load_optimizer_buffer": ([_vp, _vp, _sz], _i),
 }
 
 
@@ -187,6 +190,20 @@ class Runtime:
         arr = np.frombuffer(blob, dtype=np.uint8)
         if not lib().tkm_load_weights_buffer(self.h, _ptr(arr), arr.size):
             raise TkbError("load_weights: " + last_error())
+
+    def save_optimizer(self):
+        """SGD momentum state (TKMV layout, beside the TKM1 weights)."""
+        n = lib().tkm_runtime_optimizer_bytes(self.h)
+        buf = np.empty(max(n, 1), dtype=np.uint8)
+        size = _sz()
+        if not n or not lib().tkm_save_optimizer_buffer(self.h, _ptr(buf), n, ctypes.byref(size)):
+            raise TkbError("save_optimizer: " + last_error())
+        return buf[:n].tobytes()
+
+    def load_optimizer(self, blob):
+        arr = np.frombuffer(blob, dtype=np.uint8)
+        if not lib().tkm_load_optimizer_buffer(self.h, _ptr(arr), arr.size):
+            raise TkbError("load_optimizer: " + last_error())
 
     def grad_sample(self, node, idx):
         return float(lib().tkm_get_grad_sample(self.h, int(node), int(idx)))
