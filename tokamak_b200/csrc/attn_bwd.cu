@@ -61,7 +61,12 @@ template <int D>
 struct DkvCfg {
   static constexpr int TILE = 128 * D * 2;
   static constexpr int SLAB = 128 * 128;
-  static constexpr int NSTQ = 2;
+  // D = 64 leaves room for two S^T buffers in TMEM and four Q/dO stages: the
+  // next step's S^T is computed while this step's P^T still feeds dV, so the
+  // exponentials of consecutive steps follow each other without waiting on
+  // the tensor pipe.  D = 128 has neither (512 TMEM columns, 227 KB).
+  static constexpr bool DBL = (D == 64);
+  static constexpr int NSTQ = DBL ? 4 : 2;
   static constexpr int OFF_K = 0;
   static constexpr int OFF_V = OFF_K + TILE;
   static constexpr int OFF_Q = OFF_V + TILE;
@@ -69,11 +74,13 @@ struct DkvCfg {
   static constexpr int OFF_LSE = OFF_DO + NSTQ * TILE;  // NSTQ x 128 floats
   static constexpr int OFF_DEL = OFF_LSE + NSTQ * 512;
   static constexpr int OFF_BAR = OFF_DEL + NSTQ * 512;
-  // kv_full, q_full[NSTQ], q_empty[NSTQ], st_full, dp_full, p_ready, ds_ready, kv_done, drain
-  static constexpr int NBAR = 1 + 2 * NSTQ + 6;
+  // kv_full, q_full[NSTQ], q_empty[NSTQ], st_full[2], dp_full, p_ready, ds_ready, kv_done, drain
+  static constexpr int NBAR = 1 + 2 * NSTQ + 7;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
-  static constexpr uint32_t TM_ST = 0, TM_DP = 128, TM_DK = 256, TM_DV = 256 + D;
+  static constexpr uint32_t TM_DP = 128, TM_DK = 256, TM_DV = 256 + D;
+  // S^T buffer of step it (the second one at D = 64 only)
+  static TKB_DEVFN uint32_t tm_st(int it) { return (DBL && (it & 1)) ? 384u : 0u; }
 };
 
 template <int D, bool BF16>
@@ -86,8 +93,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + C::NSTQ;
-  uint64_t* st_full = q_empty + C::NSTQ;
-  uint64_t* dp_full = st_full + 1;
+  uint64_t* st_full = q_empty + C::NSTQ;  // [S^T buffer]
+  uint64_t* dp_full = st_full + 2;
   uint64_t* p_ready = dp_full + 1;
   uint64_t* ds_ready = p_ready + 1;
   uint64_t* kv_done = ds_ready + 1;
@@ -112,7 +119,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
-    mbar_init(st_full, 1);
+    mbar_init(&st_full[0], 1);
+    mbar_init(&st_full[1], 1);
     mbar_init(dp_full, 1);
     mbar_init(p_ready, 256);
     mbar_init(ds_ready, 256);
@@ -191,25 +199,38 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
           umma_ts(d, a_tm + half_split_col(kk), sdesc_sw128(bm + kk * 2048, C::SLAB, 1024), idKV,
                   (acc || kk > 0) ? 1u : 0u);
       };
+      // S^T of step n into its buffer; st_full[buffer] completes once per use
+      auto issue_st = [&](int n) {
+        issue_nt(tmem + C::tm_st(n), sK, sQ(n % C::NSTQ));
+        umma_commit(&st_full[C::DBL ? (n & 1) : 0]);
+      };
       bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(&q_full[0], 0, abort_flag);
       if (ok) {
         tc_fence_after();
-        issue_nt(tmem + C::TM_ST, sK, sQ(0));
-        umma_commit(st_full);
+        issue_st(0);
         issue_nt(tmem + C::TM_DP, sV, sO(0));
         umma_commit(dp_full);
+        if (C::DBL && n_steps > 1) {
+          if ((ok = mbar_wait(&q_full[1 % C::NSTQ], 0, abort_flag))) {
+            tc_fence_after();
+            issue_st(1);
+          }
+        }
       }
       for (int it = 0; ok && it < n_steps; ++it) {
         const int s = it % C::NSTQ, s1 = (it + 1) % C::NSTQ;
         const bool more = it + 1 < n_steps;
         if (!(ok = mbar_wait(p_ready, it & 1, abort_flag))) break;
         tc_fence_after();
-        issue_acc(tmem + C::TM_DV, tmem + C::TM_ST, sO(s), it > 0);           // dV += P^T dO
-        if (more) {
-          if (!(ok = mbar_wait(&q_full[s1], ((it + 1) / C::NSTQ) & 1, abort_flag))) break;
+        issue_acc(tmem + C::TM_DV, tmem + C::tm_st(it), sO(s), it > 0);       // dV += P^T dO
+        // the S^T MMA that reuses this buffer (step it + 2 with two buffers,
+        // it + 1 with one) follows the dV MMA that reads P^T from it
+        const int nxt = C::DBL ? it + 2 : it + 1;
+        if (nxt < n_steps) {
+          const int sn = nxt % C::NSTQ;
+          if (!(ok = mbar_wait(&q_full[sn], (nxt / C::NSTQ) & 1, abort_flag))) break;
           tc_fence_after();
-          issue_nt(tmem + C::TM_ST, sK, sQ(s1));                              // S^T for the next step
-          umma_commit(st_full);
+          issue_st(nxt);
         }
         if (!(ok = mbar_wait(ds_ready, it & 1, abort_flag))) break;
         tc_fence_after();
@@ -235,7 +256,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
     const bool key_ok = key < p.S;
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t cb = static_cast<uint32_t>(w * 64);
-    const uint32_t tST = tmem + lane_off + C::TM_ST + cb, tDP = tmem + lane_off + C::TM_DP + cb;
+    const uint32_t tDP = tmem + lane_off + C::TM_DP + cb;
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (int it = 0; it < n_steps; ++it) {
@@ -245,8 +266,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
       const float4* del4 = reinterpret_cast<const float4*>(smem + C::OFF_DEL + s * 512) + w * 16;
       // keys above the diagonal of a diagonal tile see no query of this half below qmin
       const int qmin = (p.causal && i == jt) ? kr - w * 64 : -1;
+      const uint32_t tST = tmem + lane_off + C::tm_st(it) + cb;
       if (!(ok = mbar_wait(&q_full[s], (it / C::NSTQ) & 1, abort_flag))) break;
-      if (!(ok = mbar_wait(st_full, it & 1, abort_flag))) break;
+      if (!(ok = mbar_wait(&st_full[C::DBL ? (it & 1) : 0], C::DBL ? ((it >> 1) & 1) : (it & 1), abort_flag))) break;
       tc_fence_after();
       uint32_t pk[32];
       {
