@@ -164,8 +164,9 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
+        # bounded: at most 6 timed and 3 warm-up samples of ~5 s each
         steps = max(1, min(args.steps, 6))
-        warm = min(args.warmup, 1)
+        warm = min(args.warmup, 3)
         v, cores, sample, t = cpu_reference(steps, warm)
         line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
                 "steps": steps, "warmup": warm, "ms_per_step": t * 1e3, "higher_is_better": True,
