@@ -188,6 +188,23 @@ static int bwd_needs_input(const TkmGraph *g, const PlasmaGroup *pg) {
 
 int tkm_group_bwd_row_inputs(const TkmGraph *g, const PlasmaGroup *pg) { return bwd_staged_rows(g, pg); }
 
+/* A normalisation group's forward (one row block per block otherwise) runs
+ * persistent with its row inputs staged two row blocks ahead by cp.async:
+ * the group input (both halves for a twin) and every Add branch. */
+int tkm_group_fwd_stage_bytes(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes) {
+    if (pg->is_qkv_prep) return 0;
+    TkmRowGeom gm;
+    tkm_row_geom(g, pg, act_bytes, &gm);
+    if (gm.persist) return 0;
+    Lists L;
+    group_lists(g, pg, &L);
+    int n = pg->is_twin_epilogue ? 2 : 1;
+    for (int i = 0; i < L.n; i++)
+        if (g->nodes[L.ids[i]].op == OP_ADD) n++;
+    const long bytes = 2L * n * gm.kch * gm.threads * 16;
+    return bytes <= 128 * 1024 ? (int)bytes : 0;
+}
+
 /* measured: staging pays for backward kernels that read several rows per row
  * (twin 0.78 -> 0.82 of HBM, norm 166 -> 163 us); one that streams dout alone
  * runs faster on plain loads (182 vs 210 us) */
@@ -757,7 +774,8 @@ static void emit_geom_macros(Em *e, int bwd) {
         bprintf(b, "#define TKG_VP %d\n#define TKG_NCH %d\n#define TKG_TPR %d\n#define TKG_KCH %d\n#define TKG_RPB %d\n"
                    "#define TKG_THREADS %d\n#define TKG_CB %d\n#define TKG_STAGE_BYTES %d\n",
                 gm->vp, gm->nch, gm->tpr, gm->kch, gm->rpb, gm->threads, gm->ncb,
-                bwd ? tkm_group_bwd_stage_bytes(e->g, e->pg, i == 0 ? 2 : 4) : 0);
+                bwd ? tkm_group_bwd_stage_bytes(e->g, e->pg, i == 0 ? 2 : 4)
+                    : tkm_group_fwd_stage_bytes(e->g, e->pg, i == 0 ? 2 : 4));
     }
     bprintf(b, "#endif\n#define TKG_C2 %d\n#define TKG_ROWS %d\n#define TKG_INV_C ", g2.C2, g2.rows);
     emit_float(b, 1.0 / (double)g2.C);
@@ -918,34 +936,68 @@ static void emit_plasma_fwd(Em *e) {
     bprintf(b, "  }\n  }\n}\n\n");
 }
 
-/* one row block per block (normalisation groups) */
+static void emit_stage_issue(Em *e, const FwdInput *rin, int nin, const char *slot_fmt, int slot_val);
+
+/* the forward chain of one row from its loaded inputs, and the store */
+static void emit_fwd_body(Em *e) {
+    Buf *b = e->b;
+    const Lists *L = &e->L;
+    if (e->pg->is_twin_epilogue) {
+        for (int i = 0; i < L->nl; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txl", 0);
+        for (int i = L->nl; i < L->nl + L->nr; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txr", 0);
+        decl_array(b, "tx");
+        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
+                   "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
+    }
+    for (int i = L->nl + L->nr; i < L->n; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "tx", 0);
+    store_array(b, A(e, KA_OUT, -1, 0), "TKG_C2", "0", "tx", 0);
+}
+
+/* Normalisation groups.  TKG_STAGE_BYTES > 0: persistent, the row inputs of
+ * the next two row blocks staged by cp.async in dynamic shared memory
+ * (tkm_group_fwd_stage_bytes); else one row block per block. */
 static void emit_plasma_fwd_rowblock(Em *e) {
     Buf *b = e->b;
     const Lists *L = &e->L;
     set_args(e, 0);
     e->acc_smem = 0;
     e->param_regs = 1;
-    kernel_head(e, "fwd", 1);
+    kernel_head(e, "fwd", 0);
     if (range_has_norm(e, 0, L->n)) bprintf(b, "  __shared__ float tkm_red[TKM_RED_SLOTS(TKG_TPR, TKG_RPB)];\n");
-    declare_stats(e);
     emit_param_preload(e);
-    const char *in = A(e, KA_IN, -1, 0);
-    if (e->pg->is_twin_epilogue) {
-        load_array(b, "txl", in, "(2 * TKG_C2)", "0");
-        load_array(b, "txr", in, "(2 * TKG_C2)", "TKG_C2");
-        emit_branch_loads(e, -1);
-        for (int i = 0; i < L->nl; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txl", 0);
-        for (int i = L->nl; i < L->nl + L->nr; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "txr", 0);
-        decl_array(b, "tx");
-        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
-                   "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
-    } else {
-        load_array(b, "tx", in, "TKG_C2", "0");
-        emit_branch_loads(e, -1);
+    FwdInput in[16];
+    const int nin = fwd_inputs(e, in);
+    bprintf(b, "#if TKG_STAGE_BYTES > 0\n"
+               "  extern __shared__ uint4 tkm_dyn[];\n"
+               "#define TKM_STG(s, a, k) tkm_dyn[(((s) * %d + (a)) * TKG_KCH + (k)) * TKG_THREADS + threadIdx.x]\n",
+            nin);
+    for (int ahead = 0; ahead < 2; ahead++) {
+        bprintf(b, "  {\n    const int rbn = blockIdx.x + %d * gridDim.x;\n", ahead);
+        emit_stage_issue(e, in, nin, "%d", ahead);
+        bprintf(b, "  }\n  tkm_cp_commit();\n");
     }
-    for (int i = L->nl + L->nr; i < L->n; i++) emit_op_fwd(e, &e->g->nodes[L->ids[i]], "tx", 0);
-    store_array(b, A(e, KA_OUT, -1, 0), "TKG_C2", "0", "tx", 0);
-    bprintf(b, "}\n\n");
+    bprintf(b, "  int tkm_it = 0;\n"
+               "  for (int tkm_rb = blockIdx.x; tkm_rb < TKG_NRB; tkm_rb += gridDim.x, ++tkm_it) {\n"
+               "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "  const bool tkm_row_ok = row < TKG_ROWS;\n"
+               "  const int tkm_sl = tkm_it & 1;\n  tkm_cp_wait<1>();\n");
+    declare_stats(e);
+    for (int i = 0; i < nin; i++) {
+        decl_array(b, in[i].arr);
+        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) tkm_lds<TKG_VP>(&TKM_STG(tkm_sl, %d, k), %s[k]);\n",
+                i, in[i].arr);
+    }
+    bprintf(b, "  {\n    const int rbn = tkm_rb + 2 * gridDim.x;\n");
+    emit_stage_issue(e, in, nin, "tkm_sl", -1);
+    bprintf(b, "  }\n  tkm_cp_commit();\n");
+    emit_fwd_body(e);
+    bprintf(b, "  }\n  tkm_cp_wait<0>();\n#undef TKM_STG\n#else\n  {\n"
+               "  const int row = blockIdx.x * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "  const bool tkm_row_ok = row < TKG_ROWS;\n");
+    declare_stats(e);
+    for (int i = 0; i < nin; i++) load_array(b, in[i].arr, in[i].src, in[i].stride, in[i].col0);
+    emit_fwd_body(e);
+    bprintf(b, "  }\n#endif\n}\n\n");
 }
 
 /* replays locals [lo, hi) on `arr`, keeping each operator's input in pre_<j>

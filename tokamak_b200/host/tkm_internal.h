@@ -77,6 +77,9 @@ int tkm_group_bwd_stage_bytes(const TkmGraph *g, const PlasmaGroup *pg, int act_
 /* row-sized inputs a plasma backward kernel reads (dout, the group input and
  * replayed Add branches when its backward needs them; a twin input counts 2) */
 int tkm_group_bwd_row_inputs(const TkmGraph *g, const PlasmaGroup *pg);
+/* dynamic shared memory of a plasma forward kernel (normalisation groups run
+ * persistent with staged rows when it is > 0) */
+int tkm_group_fwd_stage_bytes(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes);
 
 /* ------------------------------------------------ plasma kernel arguments
  * Argument list of a generated kernel (forward or backward).  The code
