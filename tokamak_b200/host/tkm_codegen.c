@@ -1103,6 +1103,36 @@ static void emit_stage_issue(Em *e, const FwdInput *rin, int nin, const char *sl
                 slot, i, rin[i].src, rin[i].stride, rin[i].col0);
 }
 
+/* backward of a group-closing RMSNorm from its input tx and dy = tg */
+static void emit_rmsnorm_last_bwd(Em *e, const TkmNode *n) {
+    Buf *b = e->b;
+    const int j = local_of(e, n->id);
+    const uint32_t f = node_flags(e->g, n->id);
+    char gm[48];
+    if (f & RES_PARAM_WEIGHT) snprintf(gm, sizeof(gm), "%s", pexpr(e, n, 0));
+    else snprintf(gm, sizeof(gm), "make_float2(1.f, 1.f)");
+    bprintf(b, "  { /* backward RMSNorm, one reduction */\n    const float eps = ");
+    emit_float(b, n->fval);
+    bprintf(b, ";\n    float2 m = make_float2(0.f, 0.f);\n");
+    pairs_begin(b);
+    bprintf(b, "          const float2 x = tx[k][q], gy = tg[k][q], gm = %s;\n"
+               "          m.x += x.x * x.x + x.y * x.y;\n"
+               "          m.y += gy.x * gm.x * x.x + gy.y * gm.y * x.y;\n",
+            gm);
+    pairs_end(b);
+    bprintf(b, "    m = tkm_row_sum2<TKG_TPR, TKG_RPB>(m, tkm_red2);\n"
+               "    const float istd = rsqrtf(m.x * TKG_INV_C + eps), m2 = istd * m.y * TKG_INV_C;\n");
+    pairs_begin(b);
+    bprintf(b, "          const float2 x = tx[k][q], gy = tg[k][q], gm = %s;\n"
+               "          const float2 xh = make_float2(x.x * istd, x.y * istd);\n",
+            gm);
+    if (f & RES_PARAM_WEIGHT)
+        bprintf(b, "          TKM_ACC(tacc_w_%d).x += gy.x * xh.x; TKM_ACC(tacc_w_%d).y += gy.y * xh.y;\n", j, j);
+    bprintf(b, "          tg[k][q] = make_float2(istd * (gy.x * gm.x - xh.x * m2), istd * (gy.y * gm.y - xh.y * m2));\n");
+    pairs_end(b);
+    bprintf(b, "  }\n");
+}
+
 static void emit_plasma_bwd(Em *e) {
     Buf *b = e->b;
     const Lists *L = &e->L;
@@ -1177,8 +1207,21 @@ static void emit_plasma_bwd(Em *e) {
         bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
                    "    tx[k][q] = make_float2(txl[k][q].x * txr[k][q].x, txl[k][q].y * txr[k][q].y);\n");
     }
-    if (need_x) emit_replay(e, L->nl + L->nr, L->n, "tx", 1);
-    emit_bwd_range(e, L->nl + L->nr, L->n, "tg");
+    const TkmNode *lastn = &e->g->nodes[L->ids[L->n - 1]];
+    int nnorm = 0;
+    for (int i = L->nl + L->nr; i < L->n; i++) nnorm += e->g->nodes[L->ids[i]].cat == CAT_NORM;
+    if (!e->pg->is_twin_epilogue && lastn->op == OP_RMSNORM && nnorm == 1) {
+        /* RMSNorm closes the group: its dy is dout, so sum(x^2) and
+         * sum(dy * gain * x) come from one row reduction (mean(dy gain xh) =
+         * istd * mean(dy gain x)) instead of the replay's and the backward's
+         * two dependent ones */
+        emit_replay(e, L->nl + L->nr, L->n - 1, "tx", 0);
+        emit_rmsnorm_last_bwd(e, lastn);
+        emit_bwd_range(e, L->nl + L->nr, L->n - 1, "tg");
+    } else {
+        if (need_x) emit_replay(e, L->nl + L->nr, L->n, "tx", 1);
+        emit_bwd_range(e, L->nl + L->nr, L->n, "tg");
+    }
     const char *din = A(e, KA_DIN, -1, 0);
     if (e->pg->is_twin_epilogue) {
         decl_array(b, "tgl");
