@@ -104,6 +104,20 @@ def test_llama_c1_bf16_step_matches_oracle():
     rt.close()
 
 
+@pytest.mark.parametrize("dtype_name", ["F32", "BF16"])
+def test_llama_layer_many_rows_matches_oracle(dtype_name):
+    """8192 rows (batch 64 x 128): more row blocks than one resident wave of
+    every kernel form (persistent, staged, one row block per block, QKV
+    prep), so a kernel that skips row blocks cannot pass."""
+    from tokamak_b200.configs import C1, dsl_for
+    rt_mod = runtime_mod()
+    dtype = getattr(rt_mod, "DTYPE_" + dtype_name)
+    cfg = dict(C1, layers=1, batch=64)
+    tols = (1e-4, 1e-4, 1e-4) if dtype_name == "F32" else (1e-2, 2e-2, 5e-2)
+    rt, *_ = compare_step(dsl_for(cfg), cfg["batch"], dtype, np.random.default_rng(21), *tols)
+    rt.close()
+
+
 def test_llama_tied_embeddings_c1():
     """Configuration 1 end to end: tied embedding matrix E (input rows are
     E[token], the head FC weight is E^T), next-token labels; dE gathers the

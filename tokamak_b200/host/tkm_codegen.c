@@ -118,7 +118,7 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
     /* measured: prefetching the next row pays for elementwise groups (twin
      * 0.69 -> 0.76, bias 0.82 -> 0.91 of HBM) but costs a normalisation the
      * resident blocks that its row reduction needs (0.65 -> 0.60) */
-    o->persist = !group_has_norm(g, pg);
+    o->persist = !group_has_norm(g, pg) && !pg->is_qkv_prep; /* the QKV prep forward is one row block per block */
 }
 
 void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *o) {
