@@ -375,411 +375,6 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
   }
 }
 
-// ============================================================================ dK / dV, P^T and dS in shared memory
-// D = 128 form of the dK/dV kernel.  TMEM holds S^T, dP^T, dK and dV (all 512
-// columns).  The compute warps write P^T (16-bit, 128-byte swizzle, K-major)
-// into a shared tile, the A operand of dV += P^T dO, and hand the S^T
-// columns back as soon as they have loaded them, so S^T of step it+1 can be
-// computed during the exponentials of step it.  Once the dV MMA has read P^T
-// the same tile takes dS in the order of the stored dS tile (see ds_tile),
-// which is a no-swizzle K-major A operand for dK += dS^T Q; two store warps
-// copy it to the dS workspace.  Q and dO have separate rings: a dO stage is
-// released by the dV MMA, a Q stage by the dK MMA.
-// Warps 0-7 compute, 8 TMA, 9 MMA, 10-11 dS stores.
-template <int D>
-struct DkvPsCfg {
-  static_assert(D == 128, "shared-memory P^T form is laid out for D = 128");
-  static constexpr int TILE = 128 * D * 2;   // 32 KB
-  static constexpr int SLAB = 128 * 128;     // 64 columns x 128 rows, 16-bit
-  static constexpr int NSTQ = 2;
-  // head area at the dynamic shared memory base (16-byte aligned)
-  static constexpr int OFF_LSE = 0;          // NSTQ x 128 floats
-  static constexpr int OFF_DEL = OFF_LSE + NSTQ * 512;
-  static constexpr int OFF_BAR = OFF_DEL + NSTQ * 512;
-  // kv_full, q_full[2], q_empty[2], o_full[2], o_empty[2], st_full, st_free,
-  // dp_full, p_ready, p_free, ds_ready, buf_free, kv_done, drain
-  static constexpr int NBAR = 1 + 4 * NSTQ + 9;
-  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int HEAD = OFF_MISC + 16;
-  // tiles, from the first 1024-byte boundary past the head area
-  static constexpr int T_K = 0, T_V = TILE, T_Q = 2 * TILE, T_DO = T_Q + NSTQ * TILE, T_P = T_DO + NSTQ * TILE;
-  static constexpr int TILES = T_P + 2 * SLAB;
-  static constexpr int SMEM = 232448;        // the per-block maximum on sm_100
-  static constexpr uint32_t TM_ST = 0, TM_DP = 128, TM_DK = 256, TM_DV = 256 + D;
-};
-
-template <int D, bool BF16>
-__global__ void __launch_bounds__(384, 1) attn_bwd_dkdv_ps_kernel(const __grid_constant__ BwdParams p) {
-  using C = DkvPsCfg<D>;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* head = smem_raw;
-  uint8_t* tiles =
-      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + C::HEAD + 1023) & ~uintptr_t(1023));
-  // The tiles fit behind the head area when the dynamic shared memory base
-  // lies within 864 bytes past a 1024-byte boundary (it is 1024-aligned on
-  // sm_100 without static shared memory).  The test is uniform over the CTA.
-  if (tiles + C::TILES > smem_raw + C::SMEM) {
-    if (threadIdx.x == 0) atomicOr(&g_device_error, ERR_BAD_LAUNCH);
-    return;
-  }
-  const uint32_t tbase = smem_u32(tiles);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(head + C::OFF_BAR);
-  uint64_t* kv_full = bars;
-  uint64_t* q_full = bars + 1;
-  uint64_t* q_empty = q_full + C::NSTQ;
-  uint64_t* o_full = q_empty + C::NSTQ;
-  uint64_t* o_empty = o_full + C::NSTQ;
-  uint64_t* st_full = o_empty + C::NSTQ;
-  uint64_t* st_free = st_full + 1;
-  uint64_t* dp_full = st_free + 1;
-  uint64_t* p_ready = dp_full + 1;
-  uint64_t* p_free = p_ready + 1;
-  uint64_t* ds_ready = p_free + 1;
-  uint64_t* buf_free = ds_ready + 1;
-  uint64_t* kv_done = buf_free + 1;
-  uint64_t* mma_drain = kv_done + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(head + C::OFF_MISC);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(head + C::OFF_MISC + 4);
-
-  const int warp = warp_id(), lane = lane_id();
-  const int BG = p.B * p.Hkv;
-  const int jt = static_cast<int>(blockIdx.x / BG);  // key tile; tile 0 sees the most queries
-  const int bg = blockIdx.x % BG;
-  const int b = bg / p.Hkv, g = bg % p.Hkv;
-  const int G = p.Hq / p.Hkv;
-  const int nq = p.S_pad >> 7;
-  const int i0 = p.causal ? jt : 0;
-  const int n_i = nq - i0;
-  const int n_steps = G * n_i;
-
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < C::NSTQ; ++s) {
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-      mbar_init(&o_full[s], 1);
-      mbar_init(&o_empty[s], 1);
-    }
-    mbar_init(st_full, 1);
-    mbar_init(st_free, 256);
-    mbar_init(dp_full, 1);
-    mbar_init(p_ready, 256);
-    mbar_init(p_free, 1);
-    mbar_init(ds_ready, 256);
-    mbar_init(buf_free, 65);  // the dK MMA's commit and the 64 threads of the dS store warps
-    mbar_init(kv_done, 1);
-    mbar_init(mma_drain, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 9) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 8) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      prefetch_tmap(&p.tmQ);
-      prefetch_tmap(&p.tmK);
-      prefetch_tmap(&p.tmV);
-      prefetch_tmap(&p.tmdO);
-      const uint64_t pol_kv = policy_evict_first(), pol_q = policy_evict_last();
-      mbar_arrive_expect_tx(kv_full, 2 * C::TILE);
-#pragma unroll
-      for (int hh = 0; hh < D / 64; ++hh) {
-        tma_load_3d(tiles + C::T_K + hh * C::SLAB, &p.tmK, kv_full, g * D + hh * 64, jt * 128, b, pol_kv);
-        tma_load_3d(tiles + C::T_V + hh * C::SLAB, &p.tmV, kv_full, g * D + hh * 64, jt * 128, b, pol_kv);
-      }
-      int iss_q = 0, iss_o = 0;
-      auto load_q = [&](int it) -> bool {
-        const int s = it % C::NSTQ;
-        const int hq = g * G + it / n_i, i = i0 + it % n_i;
-        if (!mbar_wait(&q_empty[s], ((it / C::NSTQ) & 1) ^ 1, abort_flag)) return false;
-        mbar_arrive_expect_tx(&q_full[s], C::TILE + 1024);
-#pragma unroll
-        for (int hh = 0; hh < D / 64; ++hh)
-          tma_load_3d(tiles + C::T_Q + s * C::TILE + hh * C::SLAB, &p.tmQ, &q_full[s], hq * D + hh * 64, i * 128,
-                      b, pol_q);
-        const long long ro = (static_cast<long long>(b) * p.Hq + hq) * p.S_pad + i * 128;
-        bulk_load(head + C::OFF_LSE + s * 512, p.lse2 + ro, 512, &q_full[s]);
-        bulk_load(head + C::OFF_DEL + s * 512, p.delta + ro, 512, &q_full[s]);
-        iss_q = it + 1;
-        return true;
-      };
-      auto load_o = [&](int it) -> bool {
-        const int s = it % C::NSTQ;
-        const int hq = g * G + it / n_i, i = i0 + it % n_i;
-        if (!mbar_wait(&o_empty[s], ((it / C::NSTQ) & 1) ^ 1, abort_flag)) return false;
-        mbar_arrive_expect_tx(&o_full[s], C::TILE);
-#pragma unroll
-        for (int hh = 0; hh < D / 64; ++hh)
-          tma_load_3d(tiles + C::T_DO + s * C::TILE + hh * C::SLAB, &p.tmdO, &o_full[s], hq * D + hh * 64,
-                      i * 128, b, pol_q);
-        iss_o = it + 1;
-        return true;
-      };
-      for (int it = 0; it < n_steps; ++it) {
-        // the first stages are free: Q first (S^T needs it first); later the
-        // dO stage frees before the Q stage
-        if (it < C::NSTQ) {
-          if (!load_q(it) || !load_o(it)) break;
-        } else {
-          if (!load_o(it) || !load_q(it)) break;
-        }
-      }
-      if (*abort_flag) {
-        volatile int never = 0;
-        mbar_wait(kv_full, 0, &never);
-        for (int it = max(0, iss_q - C::NSTQ); it < iss_q; ++it)
-          mbar_wait(&q_full[it % C::NSTQ], (it / C::NSTQ) & 1, &never);
-        for (int it = max(0, iss_o - C::NSTQ); it < iss_o; ++it)
-          mbar_wait(&o_full[it % C::NSTQ], (it / C::NSTQ) & 1, &never);
-      }
-    }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idS = idesc_f16kind(128, 128, BF16, false, false);  // S^T, dP^T
-      constexpr uint32_t idKV = idesc_f16kind(128, D, BF16, false, true);    // dV, dK (B MN-major)
-      const uint32_t sK = tbase + C::T_K, sV = tbase + C::T_V, sP = tbase + C::T_P;
-      auto sQ = [&](int s) { return tbase + C::T_Q + s * C::TILE; };
-      auto sO = [&](int s) { return tbase + C::T_DO + s * C::TILE; };
-      auto issue_nt = [&](uint32_t d, uint32_t a, uint32_t bm) {  // D(128x128) = A(128xD) B(128xD)^T
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::SLAB + (kk & 3) * 32;
-          umma_ss(d, sdesc_sw128(a + off, 16, 1024), sdesc_sw128(bm + off, 16, 1024), idS, kk > 0 ? 1u : 0u);
-        }
-      };
-      bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(&q_full[0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_nt(tmem + C::TM_ST, sK, sQ(0));
-        umma_commit(st_full);
-      }
-      if (ok && (ok = mbar_wait(&o_full[0], 0, abort_flag))) {
-        tc_fence_after();
-        issue_nt(tmem + C::TM_DP, sV, sO(0));
-        umma_commit(dp_full);
-      }
-      for (int it = 0; ok && it < n_steps; ++it) {
-        const int s = it % C::NSTQ, s1 = (it + 1) % C::NSTQ;
-        const uint32_t ph1 = ((it + 1) / C::NSTQ) & 1;
-        const bool more = it + 1 < n_steps;
-        // S^T of the next step goes first when its Q tile has landed by the
-        // time the compute warps hold this step's S^T in registers; otherwise
-        // dV goes first, so that the Q load does not hold up dV
-        bool st_issued = !more;
-        if (more) {
-          if (!(ok = mbar_wait(st_free, it & 1, abort_flag))) break;
-          if (mbar_try_wait(smem_u32(&q_full[s1]), ph1)) {
-            tc_fence_after();
-            issue_nt(tmem + C::TM_ST, sK, sQ(s1));
-            umma_commit(st_full);
-            st_issued = true;
-          }
-        }
-        if (!(ok = mbar_wait(p_ready, it & 1, abort_flag))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)                                        // dV += P^T dO
-          umma_ss(tmem + C::TM_DV, sdesc_sw128(sP + (kk >> 2) * C::SLAB + (kk & 3) * 32, 16, 1024),
-                  sdesc_sw128(sO(s) + kk * 2048, C::SLAB, 1024), idKV, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(p_free);
-        umma_commit(&o_empty[s]);
-        if (!st_issued) {
-          if (!(ok = mbar_wait(&q_full[s1], ph1, abort_flag))) break;
-          tc_fence_after();
-          issue_nt(tmem + C::TM_ST, sK, sQ(s1));
-          umma_commit(st_full);
-        }
-        if (!(ok = mbar_wait(ds_ready, it & 1, abort_flag))) break;
-        tc_fence_after();
-        // dK += dS^T Q; dS^T sits in the buffer in core-matrix order (no
-        // swizzle, K-major: 16 queries = two core matrices 128 bytes apart,
-        // groups of 8 keys 2048 bytes apart)
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ss(tmem + C::TM_DK, sdesc_interleave(sP + kk * 256, 128, 2048),
-                  sdesc_sw128(sQ(s) + kk * 2048, C::SLAB, 1024), idKV, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&q_empty[s]);
-        umma_commit(buf_free);
-        if (more) {
-          if (!(ok = mbar_wait(&o_full[s1], ph1, abort_flag))) break;
-          tc_fence_after();
-          issue_nt(tmem + C::TM_DP, sV, sO(s1));                             // dP^T for the next step
-          umma_commit(dp_full);
-        }
-      }
-      if (ok) umma_commit(kv_done);
-      else {
-        volatile int never = 0;
-        umma_commit(mma_drain);
-        mbar_wait(mma_drain, 0, &never);
-      }
-    }
-  } else if (warp >= 10) {
-    // ---------------------------------------------------------------- dS store warps
-    // The staged dS tile is the stored dS tile (i, jt) byte for byte; 64
-    // threads copy it with 16-byte loads and stores (each warp instruction
-    // moves 512 contiguous bytes), then release the buffer.
-    const int t = threadIdx.x - 320;
-    const uint4* src = reinterpret_cast<const uint4*>(tiles + C::T_P);
-    for (int it = 0; it < n_steps; ++it) {
-      if (!mbar_wait(ds_ready, it & 1, abort_flag)) break;
-      if (p.ds) {
-        const int hq = g * G + it / n_i, i = i0 + it % n_i;
-        const long long tile = (static_cast<long long>(b) * p.Hq + hq) * p.ds_tiles + ds_tile(i, jt, nq, p.causal);
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.ds) + tile * 32768);
-        const uint64_t pol = policy_evict_first();  // streamed once: keep Q, dO resident in L2
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          uint4 v[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) v[u] = src[(r * 8 + u) * 64 + t];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) st_global_hint(dst + (r * 8 + u) * 64 + t, v[u], pol);
-        }
-      }
-      mbar_arrive(buf_free);
-    }
-  } else {
-    // ---------------------------------------------------------------- compute warpgroups
-    const int w = warp >> 2;              // which half of the 128 query columns
-    const int kr = threadIdx.x & 127;     // key row = TMEM lane
-    const int key = jt * 128 + kr;
-    const bool key_ok = key < p.S;
-    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t cb = static_cast<uint32_t>(w * 64);
-    const uint32_t tST = tmem + lane_off + C::TM_ST + cb;
-    const uint32_t tDP = tmem + lane_off + C::TM_DP + cb;
-    // this thread's row of the P^T tile: slab w (its 64 queries), row kr,
-    // 16-byte chunk c at position c ^ (kr % 8) (128-byte swizzle) ...
-    uint8_t* prow = tiles + C::T_P + w * C::SLAB + kr * 128;
-    const int swz = kr & 7;
-    // ... and its 64 queries of dS in the same buffer, in dS tile order: byte
-    // (kr / 8) * 2048 + (q / 8) * 128 + (kr % 8) * 16 + (q % 8) * 2
-    uint8_t* drow = tiles + C::T_P + (kr >> 3) * 2048 + (kr & 7) * 16 + w * 1024;
-    const float sl2 = p.scale_log2;
-    bool ok = true;
-    for (int it = 0; it < n_steps; ++it) {
-      const int s = it % C::NSTQ;
-      const int i = i0 + it % n_i;
-      const float4* lse4 = reinterpret_cast<const float4*>(head + C::OFF_LSE + s * 512) + w * 16;
-      const float4* del4 = reinterpret_cast<const float4*>(head + C::OFF_DEL + s * 512) + w * 16;
-      // keys above the diagonal of a diagonal tile see no query of this half below qmin
-      const int qmin = (p.causal && i == jt) ? kr - w * 64 : -1;
-      if (!(ok = mbar_wait(&q_full[s], (it / C::NSTQ) & 1, abort_flag))) break;
-      if (!(ok = mbar_wait(st_full, it & 1, abort_flag))) break;
-      tc_fence_after();
-      uint32_t pk[32];
-      {
-        uint32_t v0[32], v1[32];
-        tmem_ld32(tST, v0);
-        tmem_ld32(tST + 32, v1);
-        wait_ld_dep32(v0);
-        wait_ld_dep32(v1);
-        tc_fence_before();
-        mbar_arrive(st_free);  // the S^T columns take the next step's scores
-        const bool need_mask = !key_ok || qmin > 0;
-#pragma unroll
-        for (int e4 = 0; e4 < 16; ++e4) {
-          const float4 l = lse4[e4];
-          const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
-          const int q0 = e4 * 4;
-          float a0 = ex2(fmaf(__uint_as_float(src[0]), sl2, -l.x));
-          float a1 = ex2(fmaf(__uint_as_float(src[1]), sl2, -l.y));
-          float a2 = ex2(fmaf(__uint_as_float(src[2]), sl2, -l.z));
-          float a3 = ex2(fmaf(__uint_as_float(src[3]), sl2, -l.w));
-          if (need_mask) {
-            if (!key_ok || q0 < qmin) a0 = 0.f;
-            if (!key_ok || q0 + 1 < qmin) a1 = 0.f;
-            if (!key_ok || q0 + 2 < qmin) a2 = 0.f;
-            if (!key_ok || q0 + 3 < qmin) a3 = 0.f;
-          }
-          pk[e4 * 2] = pack2<BF16>(a0, a1);
-          pk[e4 * 2 + 1] = pack2<BF16>(a2, a3);
-        }
-      }
-      // the buffer is free once the previous step's dK MMA and dS copy have
-      // read it (the dV MMA that read the previous P^T came before them)
-      if (!(ok = mbar_wait(buf_free, (it & 1) ^ 1, abort_flag))) break;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ swz) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_proxy_async_smem();
-      mbar_arrive(p_ready);
-
-      if (!(ok = mbar_wait(dp_full, it & 1, abort_flag))) break;
-      tc_fence_after();
-      uint32_t ds[32];
-      {
-        uint32_t v0[32], v1[32];
-        tmem_ld32(tDP, v0);
-        tmem_ld32(tDP + 32, v1);
-        wait_ld_dep32(v0);
-        wait_ld_dep32(v1);
-#pragma unroll
-        for (int e4 = 0; e4 < 16; ++e4) {
-          const float4 dl = del4[e4];
-          const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
-          const float2 p01 = unpack2<BF16>(pk[e4 * 2]), p23 = unpack2<BF16>(pk[e4 * 2 + 1]);
-          ds[e4 * 2] =
-              pack2<BF16>(p01.x * (__uint_as_float(src[0]) - dl.x), p01.y * (__uint_as_float(src[1]) - dl.y));
-          ds[e4 * 2 + 1] =
-              pack2<BF16>(p23.x * (__uint_as_float(src[2]) - dl.z), p23.y * (__uint_as_float(src[3]) - dl.w));
-        }
-      }
-      tc_fence_before();  // the dP^T columns take the next step's dP^T after ds_ready
-      // this step's dV MMA has read P^T: the buffer takes dS
-      if (!(ok = mbar_wait(p_free, it & 1, abort_flag))) break;
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(drow + c * 128) = make_uint4(ds[4 * c], ds[4 * c + 1], ds[4 * c + 2], ds[4 * c + 3]);
-      fence_proxy_async_smem();
-      mbar_arrive(ds_ready);
-    }
-    // epilogue: warpgroup 0 stores dK (scaled), warpgroup 1 stores dV
-    if (ok && mbar_wait(kv_done, 0, abort_flag)) {
-      tc_fence_after();
-      const float mul = w == 0 ? p.scale : 1.0f;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(w == 0 ? p.dk : p.dv) +
-                     2 * (static_cast<long long>(b) * p.dkv_batch_stride +
-                          static_cast<long long>(key) * p.dkv_row_stride + static_cast<long long>(g) * D);
-      const uint32_t src_col = w == 0 ? C::TM_DK : C::TM_DV;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_off + src_col + c * 32, v);
-        wait_ld_dep32(v);
-        uint4 o[4];
-        uint32_t* ow = reinterpret_cast<uint32_t*>(o);
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          ow[e] = pack2<BF16>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
-        if (key_ok) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 64);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) d4[e] = o[e];
-        }
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // ============================================================================ dQ
 template <int D>
 struct DqCfg {
@@ -1216,14 +811,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_const
 
 template <int D, bool BF16>
 static cudaError_t launch_bwd(const BwdParams& p, cudaStream_t stream) {
-  if constexpr (D == 128) {
-    using C = DkvPsCfg<D>;
-    auto kern = attn_bwd_dkdv_ps_kernel<D, BF16>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return e;
-    kern<<<static_cast<unsigned>(p.B * p.Hkv * (p.S_pad / 128)), 384, C::SMEM, stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  } else {
+  {
     using C = DkvCfg<D>;
     auto kern = attn_bwd_dkdv_kernel<D, BF16>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
