@@ -567,6 +567,37 @@ def run_train(args):
 # ------------------------------------------------------------- rows (C3)
 
 
+def rows_cpu_baseline():
+    """The row kernels on the host: the C oracle (a restatement of the
+    reference's semantics, fp32 in, fp64 accumulation, OpenMP) on a bounded
+    sample of the same shapes -- 2048 rows of Add+RMSNorm [x4096] and SwiGLU
+    [x11008], 1024 rows of softmax CE [x32000] -- as algorithmic bf16 bytes
+    (the byte counts the GPU line uses) over the summed time."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(0)
+    n = 2048
+    x = rng.standard_normal((n, 4096)).astype(np.float32)
+    r = rng.standard_normal((n, 4096)).astype(np.float32)
+    g = np.ones(4096, np.float32)
+    gu = rng.standard_normal((n, 2 * 11008)).astype(np.float32)
+    lg = (2.0 * rng.standard_normal((n // 2, 32000))).astype(np.float32)
+    lab = rng.integers(0, 32000, n // 2).astype(np.int32)
+    work = [(lambda: oracle.add_rmsnorm_fwd(x, r, g), 4 * n * 4096 * 2),
+            (lambda: oracle.swiglu_fwd(gu), 3 * n * 11008 * 2),
+            (lambda: oracle.softmax_loss(lg, lab), 2 * (n // 2) * 32000 * 2)]
+    tot_b, tot_t = 0, 0.0
+    for fn, nb in work:
+        fn()
+        t0 = time.perf_counter()
+        fn()
+        tot_t += time.perf_counter() - t0
+        tot_b += nb
+    return tot_b / tot_t / 1e9, oracle.num_threads(), \
+        "2048 x 4096 Add+RMSNorm fwd, 2048 x 11008 SwiGLU fwd, 1024 x 32000 softmax CE fwd+bwd"
+
+
 def run_rows(args):
     """Generated plasma kernels at configuration 2's shapes, timed per launch
     by the engine's profiler inside a bf16 training step of the graph
@@ -614,6 +645,10 @@ flow:
     if args.profile and rank == 0:
         with open(args.profile, "w") as f:
             json.dump(rows, f, indent=1)
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        v, cores, sample = rows_cpu_baseline()
+        cpu = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
         print(json.dumps({
             "metric": "fused row kernels achieved HBM GB/s (bf16)", "value": agg * world, "unit": "GB/s",
@@ -625,7 +660,7 @@ flow:
             "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": dom["GB/s"], "peak": hbm, "unit": "GB/s",
                          "frac": dom["GB/s"] / hbm, "peak_source": f"{src} HBM copy (MEASURED_PEAKS.json)",
                          "traffic": load_rows_traffic().get(dom["name"])},
-            "e2e": None, "cpu_baseline": None, "gpu_launches": len(rows)}))
+            "e2e": None, "cpu_baseline": cpu, "gpu_launches": len(rows)}))
     dist_done(world)
     return 0
 
