@@ -709,12 +709,11 @@ __global__ void __launch_bounds__(NTH) softmax_loss_kernel(const T* __restrict__
 // its registers low.  Pass 1 keeps per-thread online statistics (running max
 // m, s1 = sum e^(x-m), s2 = sum e^(2(x-m)) for the Brier score, first-index
 // argmax, the label logit); pass 2 reads the row again and writes the
-// gradient.  STAGE: the row is first brought into shared memory by one bulk
-// copy (rows of at most 72 KB, three blocks per SM), so that HBM sees one read
-// of the logits and both passes read shared memory; otherwise pass 2 re-reads
-// global memory (mostly L2) with eight rows in flight per SM.  Same results
-// as softmax_loss_kernel (src/tkm_gpu.cu:632-682).
-template <typename T, int VEC, bool STAGE>
+// gradient, re-reading global memory (mostly L2) with eight rows in flight
+// per SM.  Used for rows wider than 72 KB; narrower wide rows take
+// softmax_loss_staged_kernel.  Same results as softmax_loss_kernel
+// (src/tkm_gpu.cu:632-682).
+template <typename T, int VEC>
 __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __restrict__ logits,
                                                                   const int32_t* __restrict__ labels,
                                                                   T* __restrict__ dlogits, float* __restrict__ row_loss,
@@ -723,37 +722,13 @@ __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __res
   constexpr int NTH = 256;
   __shared__ float shm[NTH / 32], sh1[NTH / 32], sh2[NTH / 32], shx[NTH / 32];
   __shared__ int sha[NTH / 32];
-  __shared__ uint64_t row_full;
-  __shared__ int abort_flag;
-  extern __shared__ __align__(16) uint8_t stage_raw[];
-  T* stage = reinterpret_cast<T*>(stage_raw);
-  const uint32_t row_bytes = static_cast<uint32_t>(C) * sizeof(T);
   const int nvec = C / VEC;
   const float inv_rows = 1.0f / static_cast<float>(rows);
   const bool brier = kind == 2;
-  if constexpr (STAGE) {
-    if (threadIdx.x == 0) {
-      mbar_init(&row_full, 1);
-      abort_flag = 0;
-      fence_barrier_init();
-    }
-    __syncthreads();
-  }
-  int it = 0;
-  for (int row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+  for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const long long base = static_cast<long long>(row) * C;
     const int y = labels ? labels[row] : 0;
     const T* src = logits + base;
-    if constexpr (STAGE) {
-      if (threadIdx.x == 0) {
-        // the previous row's reads of the buffer (generic proxy) come first
-        fence_proxy_async_smem();
-        mbar_arrive_expect_tx(&row_full, row_bytes);
-        bulk_load(stage, logits + base, row_bytes, &row_full);
-      }
-      if (!mbar_wait(&row_full, it & 1, &abort_flag)) return;  // bounded; error word set
-      src = stage;
-    }
     float m = -INFINITY, s1 = 0.f, s2 = 0.f, xy = 0.f, best = -INFINITY;
     int arg = 0x7fffffff;
     for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
@@ -883,7 +858,165 @@ __global__ void __launch_bounds__(256) softmax_loss_stream_kernel(const T* __res
         stv<T, VEC>(dlogits + base + static_cast<long long>(vi) * VEC, o);
       }
     }
-    if constexpr (STAGE) __syncthreads();  // every read of the buffer is done before the next copy
+  }
+}
+
+// Staged form for rows of at most 72 KB: the row comes into shared memory by
+// one bulk copy (one HBM read), then three passes over shared memory:
+//   1. row max, first-index argmax and the label logit (no exponentials);
+//   2. e = e^(x - max) written back over the row in place, with sum e and
+//      sum e^2 (Brier);
+//   3. the gradient from the stored e.
+// One exponential per element instead of the streaming kernel's two (online
+// statistics, then the gradient): at 32000-wide rows the exponentials were
+// as long as the HBM traffic and did not overlap it.  The stored e is rounded
+// to T (exact for fp32); the loss uses the fp32 sums, not the stored values.
+// Same results as softmax_loss_kernel (src/tkm_gpu.cu:632-682).
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) softmax_loss_staged_kernel(const T* __restrict__ logits,
+                                                                  const int32_t* __restrict__ labels,
+                                                                  T* __restrict__ dlogits, float* __restrict__ row_loss,
+                                                                  int* __restrict__ correct, int rows, int C, int kind,
+                                                                  float gamma) {
+  constexpr int NTH = 256, NW = NTH / 32;
+  constexpr float LOG2E = 1.4426950408889634f;
+  __shared__ float shm[NW], sh1[NW], sh2[NW], shx[NW];
+  __shared__ int sha[NW];
+  __shared__ uint64_t row_full;
+  __shared__ int abort_flag;
+  extern __shared__ __align__(16) uint8_t stage_raw[];
+  T* stage = reinterpret_cast<T*>(stage_raw);
+  const uint32_t row_bytes = static_cast<uint32_t>(C) * sizeof(T);
+  const int nvec = C / VEC;
+  const float inv_rows = 1.0f / static_cast<float>(rows);
+  const bool brier = kind == 2;
+  const int warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(&row_full, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  int it = 0;
+  for (int row = blockIdx.x; row < rows; row += gridDim.x, ++it) {
+    const long long base = static_cast<long long>(row) * C;
+    const int y = labels ? labels[row] : 0;
+    if (threadIdx.x == 0) {
+      // the previous row's accesses of the buffer (generic proxy) come first
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&row_full, row_bytes);
+      bulk_load(stage, logits + base, row_bytes, &row_full);
+    }
+    if (!mbar_wait(&row_full, it & 1, &abort_flag)) return;  // bounded; error word set
+    // ---- pass 1: max, first-index argmax, label logit
+    float m = -INFINITY, xy = 0.f;
+    int arg = 0x7fffffff;
+    for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
+      float v[VEC];
+      ldv<T, VEC>(stage + vi * VEC, v);
+      float vm = v[0];
+      int va = 0;
+#pragma unroll
+      for (int e = 1; e < VEC; ++e)
+        if (v[e] > vm) { vm = v[e]; va = e; }
+      if (vm > m) { m = vm; arg = vi * VEC + va; }
+      if (y >= vi * VEC && y < vi * VEC + VEC) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (vi * VEC + e == y) xy = v[e];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o);
+      const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+      xy += __shfl_xor_sync(0xffffffffu, xy, o);
+      if (om > m || (om == m && oa < arg)) { m = om; arg = oa; }
+    }
+    if (lane == 0) {
+      shm[warp] = m;
+      sha[warp] = arg;
+      shx[warp] = xy;
+    }
+    __syncthreads();
+    float M = -INFINITY, XY = 0.f;
+    int A = 0x7fffffff;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if (shm[w] > M || (shm[w] == M && sha[w] < A)) { M = shm[w]; A = sha[w]; }
+      XY += shx[w];
+    }
+    // ---- pass 2: e = 2^(x log2e - M log2e) in place; sum e, sum e^2
+    const float nml = -M * LOG2E;
+    float s1 = 0.f, s2 = 0.f;
+    for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
+      float v[VEC];
+      ldv<T, VEC>(stage + vi * VEC, v);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        v[e] = ex2(fmaf(v[e], LOG2E, nml));
+        s1 += v[e];
+        if (brier) s2 = fmaf(v[e], v[e], s2);
+      }
+      stv<T, VEC>(stage + vi * VEC, v);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane == 0) {
+      sh1[warp] = s1;
+      sh2[warp] = s2;
+    }
+    __syncthreads();
+    float S1 = 0.f, S2 = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      S1 += sh1[w];
+      S2 += sh2[w];
+    }
+    const float inv_s = 1.0f / S1;
+    const float py_raw = exp2f((XY - M) * LOG2E) * inv_s;
+    const float pt = fmaxf(py_raw, 1e-7f);
+    const float fw = powf(1.0f - pt, gamma);
+    const float fgs = kind == 1 ? fw - gamma * pt * powf(1.0f - pt, gamma - 1.0f) * logf(pt) : 1.0f;
+    const float sum_p2 = S2 * inv_s * inv_s;
+    const float bdot = sum_p2 - py_raw;                     // sum_c p_c (p_c - t_c)
+    const float brier_sum = sum_p2 - 2.0f * py_raw + 1.0f;  // sum_c (p_c - t_c)^2
+    if (threadIdx.x == 0) {
+      float lr;
+      if (kind == 0) lr = -logf(pt) * inv_rows;
+      else if (kind == 1) lr = -fw * logf(pt) * inv_rows;
+      else lr = brier_sum / static_cast<float>(C) * inv_rows;
+      if (row_loss) row_loss[row] = lr;
+      if (correct && A == y) atomicAdd(correct, 1);
+    }
+    // ---- pass 3: gradient / rows = pc * (ga + gb * pc), minus gsub at the label
+    //   CE    pc - t                 -> ga = 1,          gb = 0,  gsub = 1
+    //   focal fgs (pc - t)           -> ga = fgs,        gb = 0,  gsub = fgs
+    //   Brier k2 pc ((pc - t) - bdot) -> ga = -k2 bdot,  gb = k2, gsub = k2 pc
+    if (dlogits) {
+      const float k2 = 2.0f / static_cast<float>(C);
+      const float ga = (kind == 0 ? 1.f : kind == 1 ? fgs : -k2 * bdot) * inv_rows;
+      const float gb = (kind == 2 ? k2 : 0.f) * inv_rows;
+      for (int vi = threadIdx.x; vi < nvec; vi += NTH) {
+        float v[VEC], o[VEC];
+        ldv<T, VEC>(stage + vi * VEC, v);  // this thread's own pass-2 values
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const float pc = v[e] * inv_s;
+          o[e] = pc * fmaf(gb, pc, ga);
+        }
+        if (y >= vi * VEC && y < vi * VEC + VEC) {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e)
+            if (vi * VEC + e == y) o[e] -= (kind == 0 ? 1.f : kind == 1 ? fgs : k2 * v[e] * inv_s) * inv_rows;
+        }
+        stv<T, VEC>(dlogits + base + static_cast<long long>(vi) * VEC, o);
+      }
+    }
+    __syncthreads();  // every access of the buffer and of the reduction slots is done before the next row
   }
 }
 
@@ -1177,13 +1310,13 @@ static cudaError_t softmax_loss_t(const void* logits, const int32_t* labels, voi
                                   float* row_loss, int rows, int C, int kind, float gamma, cudaStream_t st) {
   const size_t row_bytes = static_cast<size_t>(C) * sizeof(T);
   if (C % 8 == 0 && C >= 8192 && row_bytes <= 72 * 1024) {
-    auto kern = softmax_loss_stream_kernel<T, 8, true>;
+    auto kern = softmax_loss_staged_kernel<T, 8>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(row_bytes));
     if (e != cudaSuccess) return e;
     kern<<<row_grid(rows, 3), 256, row_bytes, st>>>((const T*)logits, labels, (T*)dlogits, row_loss, correct, rows, C,
                                                     kind, gamma);
   } else if (C % 8 == 0 && C >= 8192)
-    softmax_loss_stream_kernel<T, 8, false><<<row_grid(rows, 8), 256, 0, st>>>((const T*)logits, labels, (T*)dlogits,
+    softmax_loss_stream_kernel<T, 8><<<row_grid(rows, 8), 256, 0, st>>>((const T*)logits, labels, (T*)dlogits,
                                                                                row_loss, correct, rows, C, kind, gamma);
   else if (C % 8 == 0)
     TKB_WIDE_DISPATCH(softmax_loss_kernel, T, 8, C, rows, st, (const T*)logits, labels, (T*)dlogits, row_loss, correct,
