@@ -17,6 +17,8 @@ rows: the engine's generated plasma kernels (residual add, RMSNorm,
   timed per launch inside a training step; reported in HBM GB/s.
 longctx: long-context GQA attention fwd+bwd, B=1, 64/8 heads,
   D=128, causal, S=16384 (or --seq 32768); KV-head groups sharded over ranks.
+sweep: the attention sweep, B=8, H=16, S in {512..4096}, D in
+  {64, 128}, causal and not; every point reported.
 
 The timed region is bracketed by barriers and synchronizes, timed with CUDA
 events on the launching stream, max over ranks.  Rank 0 prints one JSON line.
@@ -150,13 +152,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="attention", choices=["attention", "train", "rows", "longctx"])
+    ap.add_argument("--workload", default="attention", choices=["attention", "train", "rows", "longctx", "sweep"])
     ap.add_argument("--seq", type=int, default=None, help="sequence length of the longctx / train workloads")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU of the train workload")
     ap.add_argument("--profile", default=None, help="write the per-launch profile (train/rows) to this JSON file")
     args = ap.parse_args()
     if args.workload != "attention":
-        return {"train": run_train, "rows": run_rows, "longctx": run_longctx}[args.workload](args)
+        return {"train": run_train, "rows": run_rows, "longctx": run_longctx, "sweep": run_sweep}[args.workload](args)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -728,6 +730,91 @@ def run_longctx(args):
                        "parallelism": f"KV-head groups sharded x{world} (no collective)"},
             "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
                          "frac": value / world / peak, "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
+                         "traffic": None},
+            "e2e": None, "cpu_baseline": None, "gpu_launches": int(L.tkb_launch_count() - n0), "clocks": clocks}))
+    dist_done(world)
+    return 0
+
+
+# ---------------------------------------------------------- sweep (C2)
+
+
+def run_sweep(args):
+    """The attention sweep of configuration 2: B=8, H=16, S in {512, 1024,
+    2048, 4096}, D in {64, 128}, causal and not, bf16, fwd+bwd through the C
+    ABI (tkb_gqa_attn_fwd + tkb_gqa_attn_bwd with the dS workspace), each point
+    timed with CUDA events over --steps steps after --warmup.  One JSON line:
+    the headline point is `value`, every point is listed under "points" with
+    its TFLOP/s and fraction of the bf16 burst peak."""
+    import ctypes
+
+    import torch
+
+    from tokamak_b200 import lib, ops
+    world, rank, local, dev = dist_setup()
+    L = lib()
+    sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    peak, peak_sus, hbm, src = load_peaks()
+    Bs, Hs = 8, 16
+    points = []
+    n0 = L.tkb_launch_count()
+    sampler = ClockSampler(local)
+    sampler.start()
+    for D_ in (64, 128):
+        for S_ in (512, 1024, 2048, 4096):
+            for causal in (1, 0):
+                g = torch.Generator(device=dev).manual_seed(5 + rank)
+                qkv = torch.randn(Bs, S_, 3 * Hs * D_, device=dev, generator=g).to(torch.bfloat16)
+                dout = torch.randn(Bs, S_, Hs * D_, device=dev, generator=g).to(torch.bfloat16)
+                out = torch.empty(Bs, S_, Hs * D_, dtype=torch.bfloat16, device=dev)
+                lse = torch.empty(Bs * Hs, S_, dtype=torch.float32, device=dev)
+                dqkv = torch.empty_like(qkv)
+                ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(Bs, S_, Hs, D_, causal, 1)
+                ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+                sc = D_ ** -0.5
+
+                def fwd():
+                    ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), Bs, S_, Hs, Hs, D_, sc, causal, 1, sp), "fwd")
+
+                def bwd():
+                    ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(dqkv), P(ws), ws_bytes, Bs, S_,
+                                                 Hs, Hs, D_, sc, causal, 1, sp), "bwd")
+                for _ in range(args.warmup):
+                    fwd()
+                    bwd()
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                dist_barrier(world)
+                ev[0].record()
+                for _ in range(args.steps):
+                    fwd()
+                ev[1].record()
+                for _ in range(args.steps):
+                    bwd()
+                ev[2].record()
+                dist_barrier(world)
+                tf = dist_max(ev[0].elapsed_time(ev[1]), world) / args.steps
+                tb = dist_max(ev[1].elapsed_time(ev[2]), world) / args.steps
+                f, b = attn_flops(Bs, Hs, S_, D_, bool(causal))
+                tot = (f + b) / ((tf + tb) * 1e-3) / 1e12
+                points.append({"S": S_, "D": D_, "causal": bool(causal), "fwd_ms": tf, "bwd_ms": tb,
+                               "fwd_tflops": f / (tf * 1e-3) / 1e12, "bwd_tflops": b / (tb * 1e-3) / 1e12,
+                               "tflops": tot, "frac": tot / peak})
+                del qkv, dout, out, lse, dqkv, ws
+    clocks = sampler.stop()
+    head = next(p_ for p_ in points if p_["S"] == 4096 and p_["D"] == 128 and p_["causal"])
+    if rank == 0:
+        print(json.dumps({
+            "metric": "attn fwd+bwd TFLOP/s sweep (bf16, B=8, H=16)", "value": head["tflops"] * world,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["fwd_ms"] + head["bwd_ms"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q,K,V,dO)",
+            "config": {"workload": "gqa_attention_sweep", "B": Bs, "H": Hs, "S": [512, 1024, 2048, 4096],
+                       "D": [64, 128], "causal": [True, False], "value_point": "S=4096, D=128, causal",
+                       "parallelism": f"replicas x{world} (no collective)"},
+            "points": points,
+            "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": peak, "unit": "TFLOP/s",
+                         "frac": head["frac"], "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
                          "traffic": None},
             "e2e": None, "cpu_baseline": None, "gpu_launches": int(L.tkb_launch_count() - n0), "clocks": clocks}))
     dist_done(world)
