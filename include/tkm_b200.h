@@ -66,7 +66,7 @@ size_t tkb_gqa_attn_bwd_workspace(int B, int S, int Hq, int D, int dtype);
 /* Workspace bytes with which tkb_gqa_attn_bwd keeps every dS tile (16-bit,
  * B * Hq * tiles * 32 KB; causal stores only the lower triangle of tiles)
  * and computes dQ as a GEMM over them instead of recomputing S, P and dP.
- * Equal to tkb_gqa_attn_bwd_workspace when that area would exceed 8 GiB.
+ * Equal to tkb_gqa_attn_bwd_workspace when that area would exceed 32 GiB.
  * Any size between the two selects the recompute path. */
 size_t tkb_gqa_attn_bwd_workspace_ex(int B, int S, int Hq, int D, int causal, int dtype);
 

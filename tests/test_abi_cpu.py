@@ -65,8 +65,12 @@ def test_workspace_sizes():
     nq = 4096 // 128
     assert L.tkb_gqa_attn_bwd_workspace_ex(8, 4096, 16, 128, 1, 1) == n + 8 * 16 * nq * (nq + 1) // 2 * 32768
     assert L.tkb_gqa_attn_bwd_workspace_ex(8, 4096, 16, 128, 0, 1) == n + 8 * 16 * nq * nq * 32768
-    # beyond 8 GiB of dS the minimum workspace is offered (dQ recomputes)
+    # beyond 32 GiB of dS the minimum workspace is offered (dQ recomputes):
+    # S=32768 with 64 heads needs 69 GB of dS, S=16384 17.3 GB (kept)
     assert L.tkb_gqa_attn_bwd_workspace_ex(1, 32768, 64, 128, 1, 1) == L.tkb_gqa_attn_bwd_workspace(1, 32768, 64, 128, 1)
+    nq16 = 16384 // 128
+    assert L.tkb_gqa_attn_bwd_workspace_ex(1, 16384, 64, 128, 1, 1) == \
+        L.tkb_gqa_attn_bwd_workspace(1, 16384, 64, 128, 1) + 64 * nq16 * (nq16 + 1) // 2 * 32768
     assert L.tkb_gqa_attn_bwd_workspace_ex(8, 4096, 16, 128, 1, 0) == 0
     assert L.tkb_add_rmsnorm_bwd_workspace(16384, 4096) > 0
     assert L.tkb_softmax_loss_workspace(8192) >= 8192 * 4

@@ -126,8 +126,10 @@ long long ds_tiles_per_head(int S, int causal) {
   return causal ? nq * (nq + 1) / 2 : nq * nq;
 }
 // Largest dS area tkb_gqa_attn_bwd_workspace_ex offers (beyond it dQ is
-// recomputed instead of read back).
-constexpr size_t kMaxDsBytes = size_t(8) << 30;
+// recomputed instead of read back).  32 GiB of the 180 GB covers the
+// long-context shape S=16384 with 64 query heads (17.3 GB; backward 14.6 ->
+// 12.8 ms against the recompute path); S=32768 (69 GB) recomputes.
+constexpr size_t kMaxDsBytes = size_t(32) << 30;
 }  // namespace
 
 extern "C" {
