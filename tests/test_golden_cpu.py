@@ -2,7 +2,7 @@
 
 tests/golden/*.npz were written by tests/golden/make_golden.py running the
 reference's own kernels and runtime (oracle/_ref/libtkm_ref.so, built from
-/root/reference/src for sm_100a) on a B200.  Inputs are fp16-exact, the
+the reference's src/ for sm_100a by oracle/build_ref.py) on a B200.  Inputs are fp16-exact, the
 reference computes in fp16 storage with fp32 accumulation (P rounded to fp16
 inside its attention), so the oracle must agree to fp16 precision:
 1e-2 relative L2 on tensors, 1e-3 relative on scalar losses.
