@@ -1,8 +1,10 @@
 """Build recipe for oracle/_ref/ -- TEST INFRASTRUCTURE ONLY.
 
-Compiles the reference (BSODsystem32/Tokamak, read-only at /root/reference)
-from its own source files where they lie, with this recipe (the reference's
-Makefile is not used).  Outputs go to oracle/_ref/ only:
+Compiles the reference (BSODsystem32/Tokamak, a read-only source tree) from
+its own source files where they lie, with this recipe (the reference's
+Makefile is not used).  The tree is found through the TKM_REFERENCE
+environment variable, else as the directory `reference` beside this
+repository.  Outputs go to oracle/_ref/ only:
 
   libtkm_ref.so       the full reference library (registry, DSL core, codegen,
                       GPU runtime) built for sm_100a plus oracle/ref_gpu_harness.cu
@@ -10,15 +12,15 @@ Makefile is not used).  Outputs go to oracle/_ref/ only:
   libtkm_ref_host.so  the host-only compiler pieces (registry, DSL core,
                       codegen) built with gcc; loads without a GPU.
 
-The GPU box has no /root/reference; the built files travel with the repo
-snapshot (oracle/_ref is git-ignored, not gpurun-ignored).
+Machines without the reference tree use the built files, which travel with
+a copy of the repository (oracle/_ref is ignored by git only).
 """
 import os
 import subprocess
 import sys
 
-REF = os.environ.get("TKM_REFERENCE", "/root/reference")
 HERE = os.path.dirname(os.path.abspath(__file__))
+REF = os.environ.get("TKM_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 OUT = os.path.join(HERE, "_ref")
 
 

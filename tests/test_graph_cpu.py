@@ -12,7 +12,9 @@ from oracle.tkm_abi import Graph, bind, compile_graph
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF_HOST = os.path.join(ROOT, "oracle", "_ref", "libtkm_ref_host.so")
-REF_MODELS = "/root/reference/models"
+from oracle.build_ref import REF  # the reference source tree (TKM_REFERENCE, else beside the repository)
+
+REF_MODELS = os.path.join(REF, "models")
 
 # Graphs written for these tests (same grammar as the reference's models).
 DSL = {
