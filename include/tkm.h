@@ -283,6 +283,35 @@ TKM_API int tkm_load_optimizer_buffer(TkmRuntime *rt, const void *buffer, size_t
 TKM_API int tkm_nccl_unique_id(void *out128);
 TKM_API int tkm_runtime_init_dp(TkmRuntime *rt, const void *unique_id128, int rank, int world_size);
 
+/* The same with the dtype the gradients cross NVLink in: 0 fp32 (what
+ * tkm_runtime_init_dp uses), 1 bf16 (each bucket is rounded to bf16 on the
+ * communication stream, averaged by NCCL in bf16 and widened back to fp32
+ * before the SGD update: half the bytes on the links). */
+TKM_API int tkm_runtime_init_dp_ex(TkmRuntime *rt, const void *unique_id128, int rank, int world_size,
+                                   int grad_dtype);
+
+/* Times the data-parallel gradient exchange alone: `iters` rounds of every
+ * bucket's all-reduce (with the bf16 conversions when selected) on the
+ * runtime's communication stream, outside the step.  The gradients are
+ * averaged in place (call it between steps, not inside one).  Writes the
+ * average milliseconds of one round to *ms_out and returns the bytes one rank
+ * sends into the all-reduce per round (0 on failure or without data
+ * parallelism). */
+TKM_API size_t tkm_runtime_dp_allreduce_time(TkmRuntime *rt, int iters, float *ms_out);
+
+/* The gradient buckets of the data-parallel step (host logic, no device
+ * state).  Inputs, per learnable tensor in registration (checkpoint) order:
+ * its value count n[t], its node id node[t] and has_grad[t] (non-zero when
+ * the step updates it; those tensors own consecutive gradient slots, each
+ * rounded up to 64 values).  Buckets are cut at node boundaries walking from
+ * the last tensor, which the backward finishes first, to the first; a bucket
+ * closes once it holds at least target_elems values.  Writes up to `cap`
+ * buckets (start node, first slot value, value count) in the order they are
+ * exchanged and returns their number; together they cover every slot once. */
+TKM_API int tkm_dp_plan_buckets(int ntens, const size_t *n, const int *node, const int *has_grad,
+                                size_t target_elems, int cap, int *bucket_node, size_t *bucket_off,
+                                size_t *bucket_len);
+
 /* Per-launch device timing of the training step: runs `iters` eager steps
  * (weights are updated with the current learning rate), timing every launch
  * of the step with CUDA events, and fills up to `capacity` entries in step

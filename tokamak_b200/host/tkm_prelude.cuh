@@ -472,6 +472,13 @@ extern "C" __global__ void __launch_bounds__(256) tkm_f32_to_bf16(const float* _
   }
 }
 
+// bf16 -> fp32 (gradients coming back from a bf16 all-reduce)
+extern "C" __global__ void __launch_bounds__(256) tkm_bf16_to_f32(const uint16_t* __restrict__ src, float* __restrict__ dst,
+                                                                  long long n) {
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256)
+    dst[i] = __uint_as_float((uint32_t)src[i] << 16);
+}
+
 // uint8 class labels (one per sample, the reference's format) -> int32 per row
 extern "C" __global__ void __launch_bounds__(256) tkm_labels_u8(const uint8_t* __restrict__ src, int n_src,
                                                                 int* __restrict__ dst, int rows) {

@@ -46,6 +46,10 @@ _SIGS = {
     "tkm_eval_current_loss": ([_vp], _f),
     "tkm_nccl_unique_id": ([_vp], _i),
     "tkm_runtime_init_dp": ([_vp, _vp, _i, _i], _i),
+    "tkm_runtime_init_dp_ex": ([_vp, _vp, _i, _i, _i], _i),
+    "tkm_runtime_dp_allreduce_time": ([_vp, _i, _c.POINTER(_f)], _sz),
+    "tkm_dp_plan_buckets": ([_i, _c.POINTER(_sz), _c.POINTER(_i), _c.POINTER(_i), _sz, _i, _c.POINTER(_i),
+                             _c.POINTER(_sz), _c.POINTER(_sz)], _i),
     "tkm_codegen_cuda_string": ([_vp], _vp),
     "tkm_runtime_profile": ([_vp, _i, _vp, _i], _i),
     "tkm_runtime_init_weights": ([_vp, _c.c_ulonglong, _f], _i),
@@ -240,10 +244,34 @@ class Runtime:
                         "backward": bool(e.backward), "bytes": e.bytes, "flops": e.flops, "ms": e.ms})
         return out
 
-    def init_dp(self, uid, rank, world):
+    def init_dp(self, uid, rank, world, grad_dtype=DTYPE_F32):
+        """Join a data-parallel group (NCCL); grad_dtype: the dtype gradients
+        are averaged in across the ranks (DTYPE_F32 or DTYPE_BF16)."""
         buf = ctypes.create_string_buffer(bytes(uid), 128)
-        if not lib().tkm_runtime_init_dp(self.h, ctypes.cast(buf, _vp), int(rank), int(world)):
+        if not lib().tkm_runtime_init_dp_ex(self.h, ctypes.cast(buf, _vp), int(rank), int(world), int(grad_dtype)):
             raise TkbError("init_dp: " + last_error())
+
+    def dp_allreduce_time(self, iters=5):
+        """(milliseconds of one round of every gradient bucket's all-reduce,
+        bytes each rank sends into it), timed alone between steps."""
+        ms = _f(0.0)
+        n = lib().tkm_runtime_dp_allreduce_time(self.h, int(iters), ctypes.byref(ms))
+        if not n:
+            raise TkbError("dp_allreduce_time: " + last_error())
+        return float(ms.value), int(n)
+
+
+def plan_buckets(sizes, nodes, has_grad, target_elems, cap=64):
+    """The engine's data-parallel gradient buckets (tkm_dp_plan_buckets) for
+    tensors in registration order: a list of (start node, first value, value
+    count) in exchange order, over the 64-value-aligned gradient slots."""
+    n = len(sizes)
+    a_n = (_sz * max(n, 1))(*[int(x) for x in sizes])
+    a_node = (_i * max(n, 1))(*[int(x) for x in nodes])
+    a_has = (_i * max(n, 1))(*[1 if x else 0 for x in has_grad])
+    bn, bo, bl = (_i * cap)(), (_sz * cap)(), (_sz * cap)()
+    k = lib().tkm_dp_plan_buckets(n, a_n, a_node, a_has, int(target_elems), int(cap), bn, bo, bl)
+    return [(bn[i], bo[i], bl[i]) for i in range(k)]
 
 
 def tkm1_pack(tensors):
