@@ -7,7 +7,12 @@ attention (default; BASELINE.json configs[1], headline shape): GQA attention
   forward + backward, bf16, causal, B=8, H=16, S=4096, D=128, through the C ABI
   of libtkm_b200.so.  One step = tkb_gqa_attn_fwd + tkb_gqa_attn_bwd.  Under
   torchrun every rank runs the same per-GPU workload (weak scaling, no
-  collective on the data path).
+  collective on the data path).  The same JSON line carries two more records
+  measured at the same N (skip them with --no-train / --no-longctx):
+    "train"    the configs[3] data-parallel training step (below) with its
+               NCCL gradient all-reduce timed alone (time, bus bandwidth);
+    "longctx"  configs[4] at S=16384 with the KV-head groups sharded over
+               the N ranks.
 train: one training step of the ~1B Llama-style decoder through
   the engine API of libtkm.so (bf16, batch 8 x 2048 tokens per GPU), the step
   captured as one CUDA graph; with N > 1 ranks the gradients are averaged by
@@ -145,7 +150,6 @@ def cpu_reference(steps, warmup, sample_heads=None):
 
 
 def main():
-    global B
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -156,19 +160,20 @@ def main():
     ap.add_argument("--seq", type=int, default=None, help="sequence length of the longctx / train workloads")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU of the train workload")
     ap.add_argument("--profile", default=None, help="write the per-launch profile (train/rows) to this JSON file")
+    ap.add_argument("--no-train", action="store_true", help="default line without the train object")
+    ap.add_argument("--no-longctx", action="store_true", help="default line without the longctx object")
+    ap.add_argument("--train-steps", type=int, default=10, help="timed steps of the train object")
+    ap.add_argument("--dp-grad-dtype", default="bf16", choices=["bf16", "fp32"],
+                    help="dtype the data-parallel gradients are averaged in")
     args = ap.parse_args()
     if args.workload != "attention":
         return {"train": run_train, "rows": run_rows, "longctx": run_longctx, "sweep": run_sweep}[args.workload](args)
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
         if rank != 0:
             return 0
-        # bounded: at most 6 timed and 3 warm-up samples of ~5 s each
-        steps = max(1, min(args.steps, 6))
-        warm = min(args.warmup, 3)
+        steps, warm = ref_sample_counts(args)
         v, cores, sample, t = cpu_reference(steps, warm)
         line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
                 "steps": steps, "warmup": warm, "ms_per_step": t * 1e3, "higher_is_better": True,
@@ -180,57 +185,71 @@ def main():
         print(json.dumps(line))
         return 0
 
+    world, rank, local, dev = dist_setup()
+    result = measure_attention(args, world, rank, local, dev)
+    if not args.no_train:
+        result["train"] = measure_train(args, world, rank, local, dev, configs_c4(args), args.train_steps,
+                                        max(3, min(args.warmup, 5)))
+    if not args.no_longctx:
+        result["longctx"] = measure_longctx(args, world, rank, local, dev, args.seq or 16384, 5, 3)
+    if rank == 0:
+        print(json.dumps(result))
+    dist_done(world)
+    return 0
+
+
+def ref_sample_counts(args):
+    """Timed and warm-up samples of the CPU reference leg: at most 6 timed and
+    3 warm-up samples of ~5 s each, in the reference arm and in the
+    cpu_baseline of the default line alike."""
+    return max(1, min(args.steps, 6)), min(args.warmup, 3)
+
+
+def measure_attention(args, world, rank, local, dev):
+    """The headline: GQA attention fwd+bwd at B=8, H=16, S=4096, D=128, causal,
+    bf16, through the C ABI; every rank runs the full per-GPU workload
+    (replicas, no collective).  Returns the JSON line (meaningful on rank 0)."""
+    import ctypes
+
     import torch
     import torch.distributed as dist
 
     from tokamak_b200 import lib
     from tokamak_b200 import ops
 
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    if args.batch:  # smaller batch for profiler captures; the bench line itself uses B=8
-        B = args.batch
+    B_ = args.batch or B  # smaller batch for profiler captures; the bench line itself uses B=8
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    qkv = torch.randn(B, S, 3 * H * D, device=dev, generator=g).to(torch.bfloat16)
-    dout = torch.randn(B, S, H * D, device=dev, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(B_, S, 3 * H * D, device=dev, generator=g).to(torch.bfloat16)
+    dout = torch.randn(B_, S, H * D, device=dev, generator=g).to(torch.bfloat16)
     sc = D ** -0.5
     L = lib()
-    ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(B, S, H, D, 1, 1)
+    ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(B_, S, H, D, 1, 1)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    out = torch.empty(B, S, H * D, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(B * H, S, dtype=torch.float32, device=dev)
+    out = torch.empty(B_, S, H * D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B_ * H, S, dtype=torch.float32, device=dev)
     dqkv = torch.empty_like(qkv)
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
-    import ctypes
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
     def fwd():
-        ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), B, S, H, H, D, sc, 1, 1, ctypes.c_void_p(sp)), "fwd")
+        ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), B_, S, H, H, D, sc, 1, 1, ctypes.c_void_p(sp)), "fwd")
 
     def bwd():
-        ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(dqkv), P(ws), ws_bytes, B, S, H, H, D, sc,
+        ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(dqkv), P(ws), ws_bytes, B_, S, H, H, D, sc,
                                      1, 1, ctypes.c_void_p(sp)), "bwd")
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
 
     for _ in range(args.warmup):
         fwd()
         bwd()
-    barrier()
+    dist_barrier(world)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
     n0 = L.tkb_launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    barrier()
+    dist_barrier(world)
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
@@ -241,7 +260,7 @@ def main():
         bwd()
         ev[i][2].record(stream)
     t_end.record(stream)
-    barrier()
+    dist_barrier(world)
     launches = L.tkb_launch_count() - n0
     clocks = sampler.stop()
     ms = t_start.elapsed_time(t_end)
@@ -251,10 +270,7 @@ def main():
     ops.check(L.tkb_device_error(ctypes.byref(code), ctypes.c_void_p(sp)), "device error query")
     if code.value:
         raise RuntimeError(f"device error word 0x{code.value:x} after the timed region")
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
+    ms = dist_max(ms, world)
 
     # e2e: host buffers in pinned memory, copies inside the timed region
     h_qkv = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
@@ -290,34 +306,31 @@ def main():
             h_out[c].copy_(out[c], non_blocking=True)
             h_dqkv[c].copy_(dqkv[c], non_blocking=True)
 
-    barrier()
+    dist_barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     up_s.wait_event(e0)
     for _ in range(e2e_steps):
-        for c in range(B):
+        for c in range(B_):
             chunk_step(c)
     tail = torch.cuda.Event()
     tail.record(down_s)
     stream.wait_event(tail)
     e1.record(stream)
-    barrier()
+    dist_barrier(world)
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
     # the chunked path returns exactly the one-call results
     ref_dqkv = torch.empty_like(dqkv)
-    ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), B, S, H, H, D, sc, 1, 1, cs), "fwd")
-    ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(ref_dqkv), P(ws), ws_bytes, B, S, H, H, D, sc,
+    ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), B_, S, H, H, D, sc, 1, 1, cs), "fwd")
+    ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(ref_dqkv), P(ws), ws_bytes, B_, S, H, H, D, sc,
                                  1, 1, cs), "bwd")
     torch.cuda.synchronize()
     e2e_identical = bool(torch.equal(ref_dqkv.cpu(), h_dqkv))
     del ref_dqkv
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
+    e2e_ms = dist_max(e2e_ms, world)
 
-    f_fl, b_fl = attn_flops(B, H, S, D, CAUSAL)
+    f_fl, b_fl = attn_flops(B_, H, S, D, CAUSAL)
     step_fl = f_fl + b_fl
     value = step_fl * world * args.steps / (ms * 1e-3) / 1e12
     e2e_value = step_fl * world / (e2e_ms * 1e-3) / 1e12
@@ -326,45 +339,41 @@ def main():
     fwd_tf = f_fl / (fwd_ms * 1e-3) / 1e12
     dom = "bwd" if bwd_ms >= fwd_ms else "fwd"
     traffic = load_traffic().get(f"attn_{dom}_bytes_per_launch")
-    result = None
-    if rank == 0:
-        cpu = None
-        if not args.no_cpu_baseline:
-            try:
-                v, cores, sample, _ = cpu_reference(1, 0, sample_heads=None)
-                cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
-            except Exception as e:  # the baseline never decides the run
-                cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {e}"}
-        result = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q,K,V,dO)",
-            "config": {"workload": "gqa_attention_fwd_bwd", "B": B, "H": H, "Hkv": H, "S": S, "D": D,
-                       "causal": CAUSAL, "per_gpu": "full workload on every rank",
-                       "l2": "inputs larger than L2 (qkv 403 MB, dqkv 403 MB)",
-                       "parallelism": f"replicas x{world} (independent batch/head units, no collective)"},
-            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "fwd_tflops": fwd_tf, "bwd_tflops": bwd_tf,
-            "roofline": {"bound": "tensor", "kernel": f"tkb_gqa_attn_{dom}", "achieved": bwd_tf if dom == "bwd" else fwd_tf,
-                         "peak": peak, "unit": "TFLOP/s",
-                         "frac": (bwd_tf if dom == "bwd" else fwd_tf) / peak,
-                         "frac_of_sustained": (bwd_tf if dom == "bwd" else fwd_tf) / peak_sus,
-                         "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)", "traffic": traffic,
-                         "flops_per_launch": b_fl if dom == "bwd" else f_fl},
-            "e2e": {"value": e2e_value, "unit": UNIT,
-                    "h2d_bytes_per_step": qkv.numel() * 2 + dout.numel() * 2,
-                    "d2h_bytes_per_step": out.numel() * 2 + dqkv.numel() * 2,
-                    "path": "pinned host -> per-sequence chunks: H2D, tkb_gqa_attn_fwd/bwd (C ABI), D2H on "
-                            "three overlapped streams -> pinned host",
-                    "matches_one_call": e2e_identical},
-            "cpu_baseline": cpu,
-            "gpu_launches": int(launches),
-            "clocks": clocks,
-        }
-        print(json.dumps(result))
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    h2d, d2h = qkv.numel() * 2 + dout.numel() * 2, out.numel() * 2 + dqkv.numel() * 2
+    del qkv, dout, out, lse, dqkv, ws, h_qkv, h_dout, h_out, h_dqkv
+    torch.cuda.empty_cache()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            steps, warm = ref_sample_counts(args)
+            v, cores, sample, _ = cpu_reference(steps, warm)
+            cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"{sample}; {warm} warm-up + {steps} timed samples, as the reference arm"}
+        except Exception as e:  # the baseline never decides the run
+            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "port", "sample": f"failed: {e}"}
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) Q,K,V,dO)",
+        "config": {"workload": "gqa_attention_fwd_bwd", "B": B_, "H": H, "Hkv": H, "S": S, "D": D,
+                   "causal": CAUSAL, "per_gpu": "full workload on every rank",
+                   "l2": "inputs larger than L2 (qkv 403 MB, dqkv 403 MB)",
+                   "parallelism": f"replicas x{world} (independent batch/head units, no collective)"},
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "fwd_tflops": fwd_tf, "bwd_tflops": bwd_tf,
+        "roofline": {"bound": "tensor", "kernel": f"tkb_gqa_attn_{dom}", "achieved": bwd_tf if dom == "bwd" else fwd_tf,
+                     "peak": peak, "unit": "TFLOP/s",
+                     "frac": (bwd_tf if dom == "bwd" else fwd_tf) / peak,
+                     "frac_of_sustained": (bwd_tf if dom == "bwd" else fwd_tf) / peak_sus,
+                     "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)", "traffic": traffic,
+                     "flops_per_launch": b_fl if dom == "bwd" else f_fl},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "pinned host -> per-sequence chunks: H2D, tkb_gqa_attn_fwd/bwd (C ABI), D2H on "
+                        "three overlapped streams -> pinned host",
+                "matches_one_call": e2e_identical},
+        "cpu_baseline": cpu,
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+    }
 
 
 # ----------------------------------------------------------------- helpers
@@ -436,34 +445,49 @@ def train_cpu_baseline(cfg):
         f"1 layer of configuration 4 (d 2048, GQA 32/8x64, FFN 5632, vocab 32000), 1 x 256 tokens, fwd+bwd, float64"
 
 
-def run_train(args):
+def configs_c4(args):
+    from tokamak_b200 import configs
+    cfg = dict(configs.C4)
+    if args.workload == "train":  # the overrides serve profiling runs of the train workload only
+        if args.seq:
+            cfg["seq"] = args.seq
+        if args.batch:
+            cfg["batch"] = args.batch
+    return cfg
+
+
+def measure_train(args, world, rank, local, dev, cfg, steps, warmup):
+    """Configuration 4: one training step of the ~1B Llama-style decoder
+    through the engine API (libtkm.so), bf16, the whole step one CUDA graph;
+    at N ranks data parallel with the gradients averaged by NCCL all-reduces
+    inside the graph (weak scaling: 8 x 2048 tokens per GPU).  Returns the
+    `train` record (meaningful on rank 0)."""
     import ctypes
+    import hashlib
 
     import numpy as np
     import torch
     import torch.distributed as dist
 
     from tokamak_b200 import configs, runtime
-    world, rank, local, dev = dist_setup()
-    cfg = dict(configs.C4)
-    if args.seq:
-        cfg["seq"] = args.seq
-    if args.batch:
-        cfg["batch"] = args.batch
-    B, T, d, V = cfg["batch"], cfg["seq"], cfg["d_model"], cfg["vocab"]
-    rt = runtime.Runtime.from_dsl(configs.dsl_for(cfg), B, runtime.DTYPE_BF16)
+    B_, T, d, V = cfg["batch"], cfg["seq"], cfg["d_model"], cfg["vocab"]
+    grad_dtype = runtime.DTYPE_BF16 if args.dp_grad_dtype == "bf16" else runtime.DTYPE_F32
+    t_ign = time.perf_counter()
+    rt = runtime.Runtime.from_dsl(configs.dsl_for(cfg), B_, runtime.DTYPE_BF16)
     rt.init_weights(1234, 0.02)
     if world > 1:
         obj = [runtime.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
-        rt.init_dp(obj[0], rank, world)
+        rt.init_dp(obj[0], rank, world, grad_dtype)
+    ignite_s = time.perf_counter() - t_ign
     # synthetic tokens: rows are the embeddings of uniform token ids (a
     # seeded N(0, 0.02) table), labels the next token
     g = np.random.default_rng(100 + rank)
     table = g.normal(0.0, 0.02, (V, d)).astype(np.float32)
-    tokens = g.integers(0, V, (B, T + 1))
+    tokens = g.integers(0, V, (B_, T + 1))
     x = torch.from_numpy(table[tokens[:, :-1]].reshape(-1)).pin_memory()
     y = torch.from_numpy(tokens[:, 1:].reshape(-1).astype(np.int32)).pin_memory()
+    del table
     L = runtime.lib()
     lr = 1e-4
 
@@ -475,40 +499,66 @@ def run_train(args):
 
     first = step_e2e()  # uploads this rank's batch, runs eagerly, captures the step graph
     stream = torch.cuda.ExternalStream(rt.stream)
-    for _ in range(max(0, args.warmup - 1)):
+    for _ in range(max(0, warmup - 1)):
         rt.step_resident(lr)
-    dist_barrier(world)
     stream.synchronize()
+    dist_barrier(world)
     sampler = ClockSampler(local)
     sampler.start()
     time.sleep(0.3)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist_barrier(world)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         rt.step_resident(lr)
     e1.record(stream)
     stream.synchronize()
     dist_barrier(world)
     clocks = sampler.stop()
     ms = dist_max(e0.elapsed_time(e1), world)
+
+    # the gradient exchange alone (all ranks together, between steps)
+    allreduce = None
+    if world > 1:
+        dist_barrier(world)
+        ar_ms, ar_bytes = rt.dp_allreduce_time(5)
+        ar_ms = dist_max(ar_ms, world)
+        algbw = ar_bytes / (ar_ms * 1e-3) / 1e9
+        allreduce = {"ms": ar_ms, "bytes_per_rank": ar_bytes, "dtype": args.dp_grad_dtype,
+                     "algbw_GBs": algbw, "busbw_GBs": algbw * 2 * (world - 1) / world,
+                     "link_ref_GBs": 770.0, "collective": "ncclAllReduce(avg), ~16 buckets in reverse layer order",
+                     "overlap": "issued on a second stream as the backward completes each bucket; "
+                                "the SGD update waits for the last"}
+
     # end to end: pinned host embeddings + labels uploaded every step, loss read back
-    e2e_steps = max(2, min(args.steps, 4))
+    e2e_steps = 4
+    host_ms = []
     dist_barrier(world)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
     last = first
     for _ in range(e2e_steps):
+        h0 = time.perf_counter()
         last = step_e2e()
+        host_ms.append((time.perf_counter() - h0) * 1e3)
     t1.record(stream)
     stream.synchronize()
     e2e_ms = dist_max(t0.elapsed_time(t1) / e2e_steps, world)
-    tokens_step = B * T
-    value = tokens_step * world * args.steps / (ms * 1e-3)
+    # what one step's upload costs when every rank uploads at once
+    dbuf = torch.empty(x.numel(), dtype=torch.float32, device=dev)
+    dist_barrier(world)
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    u0.record()
+    dbuf.copy_(x, non_blocking=True)
+    u1.record()
+    torch.cuda.synchronize()
+    up_ms = dist_max(u0.elapsed_time(u1), world)
+    del dbuf
+    tokens_step = B_ * T
+    value = tokens_step * world * steps / (ms * 1e-3)
     e2e_value = tokens_step * world / (e2e_ms * 1e-3)
     # data parallel: every rank must hold the same weights after the steps
-    import hashlib
     digest = hashlib.sha256(rt.save_weights()).hexdigest()
     digests = [None] * world
     if world > 1:
@@ -516,52 +566,66 @@ def run_train(args):
     else:
         digests = [digest]
     prof = None
-    if rank == 0 and args.profile:
+    if rank == 0 and args.profile and args.workload == "train":
         prof = rt.profile(iters=2)
         with open(args.profile, "w") as f:
             json.dump(prof, f)
     # model FLOPs of one step: every GEMM (forward 2, backward 4 per MAC) plus attention
     L_, q, kv, hd, F = cfg["layers"], cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["ffn"]
     gemm_macs = L_ * d * (q * hd + 2 * kv * hd + q * hd + 3 * F) + d * V
-    attn = L_ * 4.0 * B * q * T * T * hd * 0.5 * 3.5
+    attn = L_ * 4.0 * B_ * q * T * T * hd * 0.5 * 3.5
     step_flops = 6.0 * tokens_step * gemm_macs + attn
     peak, peak_sus, hbm, src = load_peaks()
-    achieved = step_flops / (ms / args.steps * 1e-3) / 1e12
+    achieved = step_flops / (ms / steps * 1e-3) / 1e12
+    rt.close()
+    torch.cuda.empty_cache()
+    rec = {
+        "metric": "train tokens/sec (Llama-style ~1B, bf16, data parallel)", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+        "tokens_per_s_per_gpu": value / world, "higher_is_better": True, "scaling": "weak",
+        "dtype": "bf16", "data": "synthetic (seeded uniform token ids, N(0,0.02) embeddings and weights)",
+        "config": {"workload": "llama_1b_train_step", "layers": L_, "d_model": d, "heads": f"{q}/{kv}x{hd}",
+                   "ffn": F, "vocab": V, "seq_len": T, "micro_batch": B_, "global_batch": B_ * world,
+                   "parallelism": f"dp{world}", "graph": "whole step captured as one CUDA graph",
+                   "grad_allreduce_dtype": args.dp_grad_dtype if world > 1 else None,
+                   "l2": "working set far above L2 (activations ~40 GB)"},
+        "ignite_s": ignite_s, "loss_first_step": first, "loss_last": last,
+        "dp_weights_identical_across_ranks": len(set(digests)) == 1, "weights_sha256": digests[0][:16],
+        "allreduce": allreduce,
+        "roofline": {"bound": "tensor", "kernel": "whole step (GEMM + attention FLOPs)", "achieved": achieved,
+                     "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
+                     "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json)", "traffic": None,
+                     "flops_per_step_per_gpu": step_flops},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 4 + y.numel() * 4,
+                "d2h_bytes_per_step": 4, "path": "pinned host -> tkm_runtime_step_i32 (engine C API) -> loss",
+                "host_ms_per_call": host_ms, "upload_ms_all_ranks_at_once": up_ms},
+        "clocks": clocks,
+    }
+    if prof:
+        by_kind = {}
+        for e in prof:
+            by_kind[e["kind"]] = by_kind.get(e["kind"], 0.0) + e["ms"]
+        rec["profile_ms_by_kind"] = by_kind
+        rec["gpu_launches"] = len(prof)
+    return rec
+
+
+def run_train(args):
+    world, rank, local, dev = dist_setup()
+    cfg = configs_c4(args)
+    line = measure_train(args, world, rank, local, dev, cfg, args.steps, args.warmup)
     if rank == 0:
         cpu = None
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             try:
                 v, cores, sample = train_cpu_baseline(cfg)
                 cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
             except Exception as e:
                 cpu = {"value": None, "unit": "tokens/s", "cores": None, "kind": "port", "sample": f"failed: {e}"}
-        line = {
-            "metric": "train tokens/sec (Llama-style ~1B, bf16, data parallel)", "value": value, "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded uniform token ids, N(0,0.02) embeddings and weights)",
-            "config": {"workload": "llama_1b_train_step", "layers": L_, "d_model": d, "heads": f"{q}/{kv}x{hd}",
-                       "ffn": F, "vocab": V, "seq_len": T, "micro_batch": B, "global_batch": B * world,
-                       "parallelism": f"dp{world}", "graph": "whole step captured as one CUDA graph",
-                       "l2": "working set far above L2 (activations ~40 GB)"},
-            "loss_first_step": first, "loss_last": last,
-            "dp_weights_identical_across_ranks": len(set(digests)) == 1,
-            "roofline": {"bound": "tensor", "kernel": "whole step (GEMM + attention FLOPs)", "achieved": achieved,
-                         "peak": peak_sus, "unit": "TFLOP/s", "frac": achieved / peak_sus,
-                         "peak_source": f"{src} bf16 sustained (MEASURED_PEAKS.json)", "traffic": None,
-                         "flops_per_step": step_flops},
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 4 + y.numel() * 4,
-                    "d2h_bytes_per_step": 4, "path": "pinned host -> tkm_runtime_step_i32 (engine C API) -> loss"},
-            "cpu_baseline": cpu, "gpu_launches": None, "clocks": clocks,
-        }
-        if prof:
-            by_kind = {}
-            for e in prof:
-                by_kind[e["kind"]] = by_kind.get(e["kind"], 0.0) + e["ms"]
-            line["profile_ms_by_kind"] = by_kind
-            line["gpu_launches"] = len(prof)
+        line["vs_baseline"] = None
+        line["cpu_baseline"] = cpu
+        line.setdefault("gpu_launches", None)
         print(json.dumps(line))
-    rt.close()
     dist_done(world)
     return 0
 
@@ -670,38 +734,40 @@ flow:
 # ---------------------------------------------------------- longctx (C5)
 
 
-def run_longctx(args):
+def measure_longctx(args, world, rank, local, dev, S_, steps, warmup):
+    """Configuration 5: long-context GQA attention fwd+bwd, B=1, 64/8 heads,
+    D=128, causal, bf16; the 8 KV-head groups (each with its 8 query heads)
+    sharded over the ranks with no collective (strong scaling: the total work
+    is fixed).  Returns the `longctx` record (meaningful on rank 0)."""
     import ctypes
 
     import torch
 
     from tokamak_b200 import lib, ops
-    world, rank, local, dev = dist_setup()
-    S = args.seq or 16384
-    Hq_all, Hkv_all, D = 64, 8, 128
+    Hq_all, Hkv_all, D_ = 64, 8, 128
     if Hkv_all % world:
         raise SystemExit("KV-head groups (8) must divide over the ranks")
     Hkv = Hkv_all // world
     Hq = Hq_all // world
     g = torch.Generator(device=dev).manual_seed(77 + rank)
-    qkv = torch.randn(1, S, (Hq + 2 * Hkv) * D, device=dev, generator=g).to(torch.bfloat16)
-    dout = torch.randn(1, S, Hq * D, device=dev, generator=g).to(torch.bfloat16)
-    out = torch.empty(1, S, Hq * D, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(Hq, S, dtype=torch.float32, device=dev)
+    qkv = torch.randn(1, S_, (Hq + 2 * Hkv) * D_, device=dev, generator=g).to(torch.bfloat16)
+    dout = torch.randn(1, S_, Hq * D_, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(1, S_, Hq * D_, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(Hq, S_, dtype=torch.float32, device=dev)
     dqkv = torch.empty_like(qkv)
     L = lib()
-    ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(1, S, Hq, D, 1, 1)
+    ws_bytes = L.tkb_gqa_attn_bwd_workspace_ex(1, S_, Hq, D_, 1, 1)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    sc = D ** -0.5
+    sc = D_ ** -0.5
     sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
     def step():
-        ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), 1, S, Hq, Hkv, D, sc, 1, 1, sp), "fwd")
-        ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(dqkv), P(ws), ws_bytes, 1, S, Hq, Hkv, D,
+        ops.check(L.tkb_gqa_attn_fwd(P(qkv), P(out), P(lse), 1, S_, Hq, Hkv, D_, sc, 1, 1, sp), "fwd")
+        ops.check(L.tkb_gqa_attn_bwd(P(qkv), P(out), P(dout), P(lse), P(dqkv), P(ws), ws_bytes, 1, S_, Hq, Hkv, D_,
                                      sc, 1, 1, sp), "bwd")
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     dist_barrier(world)
     sampler = ClockSampler(local)
@@ -711,27 +777,39 @@ def run_longctx(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist_barrier(world)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record()
     dist_barrier(world)
     clocks = sampler.stop()
+    launches = int(L.tkb_launch_count() - n0)
     ms = dist_max(e0.elapsed_time(e1), world)
-    f, b = attn_flops(1, Hq, S, D, True)
-    value = (f + b) * world * args.steps / (ms * 1e-3) / 1e12
+    f, b = attn_flops(1, Hq, S_, D_, True)
+    value = (f + b) * world * steps / (ms * 1e-3) / 1e12
     peak, peak_sus, hbm, src = load_peaks()
+    del qkv, dout, out, lse, dqkv, ws
+    torch.cuda.empty_cache()
+    return {
+        "metric": "long-context GQA attn fwd+bwd TFLOP/s (bf16, causal)", "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps,
+        "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "gqa_attention_long_context", "B": 1, "Hq": Hq_all, "Hkv": Hkv_all, "S": S_, "D": D_,
+                   "causal": True, "per_gpu": f"{Hq} query / {Hkv} KV heads",
+                   "parallelism": f"KV-head groups sharded x{world} (no collective)",
+                   "dS_workspace": ws_bytes > L.tkb_gqa_attn_bwd_workspace(1, S_, Hq, D_, 1)},
+        "per_gpu_tflops": value / world,
+        "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
+                     "frac": value / world / peak, "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
+                     "traffic": None},
+        "gpu_launches": launches, "clocks": clocks}
+
+
+def run_longctx(args):
+    world, rank, local, dev = dist_setup()
+    line = measure_longctx(args, world, rank, local, dev, args.seq or 16384, args.steps, args.warmup)
     if rank == 0:
-        print(json.dumps({
-            "metric": "long-context GQA attn fwd+bwd TFLOP/s (bf16, causal)", "value": value, "unit": "TFLOP/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "gqa_attention_long_context", "B": 1, "Hq": Hq_all, "Hkv": Hkv_all, "S": S, "D": D,
-                       "causal": True, "per_gpu": f"{Hq} query / {Hkv} KV heads",
-                       "parallelism": f"KV-head groups sharded x{world} (no collective)"},
-            "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
-                         "frac": value / world / peak, "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)",
-                         "traffic": None},
-            "e2e": None, "cpu_baseline": None, "gpu_launches": int(L.tkb_launch_count() - n0), "clocks": clocks}))
+        line.update({"vs_baseline": None, "e2e": None, "cpu_baseline": None})
+        print(json.dumps(line))
     dist_done(world)
     return 0
 
