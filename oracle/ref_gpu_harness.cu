@@ -61,4 +61,54 @@ int ref_softmax_bwd(const void* p, const void* dp, void* dx, int rows, int cols,
   return (int)cudaGetLastError();
 }
 
+// Launch site src/tkm_gpu.cu:1417-1420, with the tensor table the runtime
+// uploads at src/tkm_gpu.cu:1127 (SgdTensorList in constant memory).  The
+// pointer arrays are host arrays of device pointers; fp16[i] may be null.
+int ref_sgd(float* const* master, __half* const* fp16, float* const* vel, const float* const* grad,
+            const int* sizes, int count, const float* d_lr, float momentum, float wd, uint32_t* d_seed,
+            void* stream) {
+  if (count <= 0 || count > TKM_MAX_TENSORS) return -1;
+  SgdTensorList h;
+  memset(&h, 0, sizeof(h));
+  h.count = count;
+  for (int i = 0; i < count; i++) {
+    h.master[i] = master[i];
+    h.fp16_w[i] = fp16[i];
+    h.vel[i] = vel[i];
+    h.grad[i] = grad[i];
+    h.size[i] = sizes[i];
+    h.offset[i + 1] = h.offset[i] + sizes[i];
+  }
+  cudaError_t e = cudaMemcpyToSymbol(c_tkm_sgd, &h, sizeof(SgdTensorList));
+  if (e != cudaSuccess) return (int)e;
+  const int total = h.offset[count];
+  k_tkm_multi_tensor_sgd<<<(total + 255) / 256, 256, 0, (cudaStream_t)stream>>>(d_lr, momentum, wd, d_seed);
+  return (int)cudaGetLastError();
+}
+
+// The fused QKV-prep group of a reference runtime after a forward pass: the
+// node ids of the fused [Q|K|V] GEMM (the group's input) and of the prep node
+// (src/tkm_registry.c:701-770 rewrites the Q chain's first node into it), and
+// their fp16 activations copied to host buffers of `elems` halves each.
+int ref_qkv_prep_acts(TkmRuntime* rt, int* gemm_id, int* prep_id, void* h_in, void* h_out, size_t elems) {
+  const TkmGraph* g = &rt->graph;
+  int prep = -1;
+  for (int i = 0; i < g->num_nodes; i++)
+    if (!g->nodes[i].dead && g->nodes[i].op == OP_QKNORM && g->nodes[i].in0 >= 0 &&
+        g->nodes[g->nodes[i].in0].op == OP_FC_QKV_FUSED)
+      prep = i;
+  if (prep < 0) return -1;
+  const TkmNode* pn = &g->nodes[prep];
+  const TkmNode* fn = &g->nodes[pn->in0];
+  const size_t need = (size_t)g->batch_size * pn->H * pn->W * pn->c_out;
+  if (need != elems) return -2;
+  cudaDeviceSynchronize();
+  cudaError_t e = cudaMemcpy(h_in, rt->d_arena + fn->out_offset, elems * sizeof(__half), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(h_out, rt->d_arena + pn->out_offset, elems * sizeof(__half), cudaMemcpyDeviceToHost);
+  *gemm_id = fn->id;
+  *prep_id = prep;
+  return (int)e;
+}
+
 }  // extern "C"

@@ -123,3 +123,51 @@ def test_silu_residual_matches_reference_runtime():
     gu = np.concatenate([x, np.ones_like(x)], 1).astype(np.float32)
     h = oracle.swiglu_fwd(np.ascontiguousarray(gu))
     assert rel_l2(h + x, z["y"].reshape(-1, 64)) < 2e-3
+
+
+@pytest.mark.parametrize("path", files("qkvprep_"))
+def test_qkv_prep_matches_reference_runtime(path):
+    """The reference runtime's fused QKV-prep group (bias, optional per-head
+    QKNorm, RoPE on the Q and K channels; src/tkm_codegen.c:43-70, 211-295)
+    inside a GQA graph, fed with the fused GEMM output it saw.  The bias and
+    the QKNorm gain come from the TKM1 weights the reference ran with, found
+    through the graph's tensor registration order.  The reference stores fp16
+    and uses fast-math exponentials and sincos, so the bound is fp16-level;
+    a different pair convention or frequency rule is off by O(1)."""
+    from oracle.graph_oracle import oracle_for, reference_front_end
+    from tokamak_b200.runtime import tkm1_unpack
+    z = np.load(path)
+    S, Hq, Hkv, D, qkn = (int(v) for v in z["shape"])
+    front = reference_front_end()
+    if front is None:
+        pytest.skip("reference host library not built (oracle/build_ref.py)")
+    orc = oracle_for(str(z["dsl"]), int(z["batch"]), front)
+    tensors = tkm1_unpack(z["weights"].tobytes())
+    assert [t.size for t in tensors] == [n for _, _, n in orc.tensors]
+    pid = int(z["prep_node"])
+    bias = tensors[orc.tidx[(pid, 3)]]
+    gain = tensors[orc.tidx[(pid, 1)]]
+    rope = dict(zip(("theta", "scale", "low", "high", "octx"), (float(v) for v in z["rope"])))
+    out, _ = oracle.qkv_prep_fwd(z["prep_in"], bias, gain, S, Hq, Hkv, D, bool(qkn), True, **rope)
+    ref = z["prep_out"]
+    assert rel_l2(out, ref) < 2e-3
+    assert np.abs(out - ref).max() < 1e-2 * np.abs(ref).max()
+    # V channels pass through with the bias only
+    qk = (Hq + Hkv) * D
+    assert np.abs(out[:, qk:] - ref[:, qk:]).max() <= 2e-3 * np.abs(ref[:, qk:]).max()
+
+
+def test_sgd_matches_reference_kernel():
+    """k_tkm_multi_tensor_sgd (src/tkm_gpu.cu:695-720) on three tensors: the
+    oracle repeats its fmaf chain, so masters and velocities agree bit for
+    bit; the fp16 GEMM copy is the master rounded to nearest; the seed
+    advances by 0x9E3779B9."""
+    z = np.load(os.path.join(GOLD, "sgd.npz"))
+    lr, mom, wd = float(z["lr"]), float(z["momentum"]), float(z["wd"])
+    for i, has16 in enumerate(z["fp16_copy"]):
+        p, v = oracle.sgd(z[f"p0_{i}"], z[f"v0_{i}"], z[f"g_{i}"], lr, mom, wd, apply_wd=bool(has16))
+        assert np.array_equal(p, z[f"p1_{i}"]), i
+        assert np.array_equal(v, z[f"v1_{i}"]), i
+        if has16:
+            assert np.array_equal(p.astype(np.float16).astype(np.float32), z[f"h1_{i}"])
+    assert int(z["seed_out"]) == (int(z["seed_in"]) + 0x9E3779B9) & 0xFFFFFFFF
