@@ -23,7 +23,8 @@ def source_of(dsl, batch):
     return ctypes.string_at(p).decode(), g
 
 
-@pytest.mark.parametrize("name", ["llama_c1", "gqa_qknorm_rope_scaled", "twin_custom", "image_like", "rules"])
+@pytest.mark.parametrize("name", ["llama_c1", "gqa_qknorm_rope_scaled", "twin_custom", "image_like", "rules",
+                                  "residual_of_input"])
 @pytest.mark.parametrize("act_bytes", [2, 4])
 def test_generated_code_compiles_for_sm100a(name, act_bytes):
     src, _ = source_of(DSL[name], 4)
@@ -43,3 +44,13 @@ def test_identical_layers_share_kernels():
 def test_unsupported_groups_are_reported():
     src, _ = source_of("input: 8x8x4\nflow:\n  a: RandFlipX -> RandNoise -> FC(10) -> SoftmaxCE\n", 2)
     assert "#error" in src and "augmentation" in src
+
+
+def test_residual_of_group_input_sums_before_one_store():
+    """A residual whose skip is the group's own input: the Add branch
+    gradient and d(input) share one slot, so the backward sums them in
+    registers and stores once (no second write through an aliasing pointer)."""
+    src, _ = source_of(DSL["residual_of_input"], 4)
+    bwd = src[src.index("TKM_KNAME(bwd)"):]
+    assert "tdbr" in bwd
+    assert "tkm_st<TKG_VP>(a" in bwd or "tkm_st_add<TKG_VP>(a" in bwd

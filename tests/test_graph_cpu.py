@@ -87,6 +87,15 @@ flow:
   s: Flatten -> FC(32) -> LeakyReLU(0.2) -> ELU -> HardSigmoid -> Sigmoid -> SwishBeta -> Sin(2.0) -> Clamp(3)
   h: FC(10) -> SoftmaxCE
 """,
+    "residual_of_input": """
+input: 1x16x64
+flow:
+  r: {
+    branch: SiLU -> Scale(0.5)
+    skip: Identity
+  } -> Add
+  n: RMSNorm -> FC(8) -> SoftmaxCE
+""",
 }
 
 

@@ -74,6 +74,7 @@ def compare_step(dsl, batch, dtype, rng, tol_loss, tol_logits, tol_grad, labels_
         e = rel_l2(g, want)
         worst = max(worst, e)
         assert e <= tol_grad, (t, node, kind, e)
+    print(f"[compare_step] worst parameter-gradient rel L2 {worst:.4g}")
     return rt, orc, params, ref, worst
 
 
@@ -351,3 +352,16 @@ def test_rejects_bad_labels_and_foreign_source():
     h = R.lib().tkm_runtime_ignite(ctypes.cast(ctypes.pointer(g), ctypes.c_void_p), b"extern \"C\" __global__ void k(){}")
     assert not h
     assert "tkm_codegen_cuda_string" in R.last_error()
+
+
+@pytest.mark.parametrize("dtype_name", ["F32", "BF16"])
+def test_residual_whose_skip_is_the_group_input(dtype_name):
+    """{ branch: SiLU -> Scale, skip: Identity } -> Add -> RMSNorm on the
+    graph input: d(input) gets the skip's gradient and the branch's from one
+    fused backward kernel."""
+    from test_graph_cpu import DSL
+    rt_mod = runtime_mod()
+    dtype = getattr(rt_mod, "DTYPE_" + dtype_name)
+    tols = (1e-4, 1e-4, 1e-4) if dtype_name == "F32" else (1e-2, 2e-2, 2e-2)
+    rt, *_ = compare_step(DSL["residual_of_input"], 8, dtype, np.random.default_rng(31), *tols)
+    rt.close()

@@ -680,6 +680,25 @@ static void emit_op_fwd(Em *e, const TkmNode *n, const char *arr, int replay) {
     bprintf(b, "  }\n");
 }
 
+/* Does Add node n's branch gradient land in the same slot as the group's own
+ * input gradient (a residual whose skip is the group input)?  Both writes then
+ * target one buffer: the kernel sums them in registers and stores once,
+ * instead of two stores through pointers the compiler may reorder. */
+static int add_aliases_din(const Em *e, const TkmNode *n) {
+    return n->op == OP_ADD && !e->pg->is_twin_epilogue &&
+           tkm_slot_of(e->g, n->in1) == tkm_slot_of(e->g, e->pg->anchor_id);
+}
+
+/* the first planned write among the aliased Add branches (the backward
+ * plans a group's Adds from its last operator), or -1 */
+static int first_aliased_add(const Em *e) {
+    for (int j = e->pg->count - 1; j >= 0; j--) {
+        const TkmNode *n = &e->g->nodes[e->pg->node_ids[j]];
+        if (add_aliases_din(e, n)) return n->id;
+    }
+    return -1;
+}
+
 /* backward of operator n: `dy` array updated in place, `pre` = its input */
 static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
     Buf *b = e->b;
@@ -714,7 +733,12 @@ static void emit_op_bwd(Em *e, const TkmNode *n, const char *dy) {
         pairs_end(b);
     } else if (n->op == OP_ADD) {
         /* the branch receives the incoming gradient; the main path keeps it */
-        store_array(b, A(e, KA_DBRANCH, n->id, 0), "TKG_C2", "0", dy, e->plan->add_branch_acc[n->id] > 0);
+        if (add_aliases_din(e, n))
+            bprintf(b, "    _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+                       "      tdbr[k][q].x += %s[k][q].x; tdbr[k][q].y += %s[k][q].y;\n    }\n",
+                    dy, dy);
+        else
+            store_array(b, A(e, KA_DBRANCH, n->id, 0), "TKG_C2", "0", dy, e->plan->add_branch_acc[n->id] > 0);
     } else if (n->op == OP_BIAS) {
         pairs_begin(b);
         bprintf(b, "          TKM_ACC(tacc_b_%d).x += %s[k][q].x; TKM_ACC(tacc_b_%d).y += %s[k][q].y;\n", j, dy, j, dy);
@@ -1203,6 +1227,11 @@ static void emit_plasma_bwd(Em *e) {
                "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
                "  const bool tkm_row_ok = row < TKG_ROWS;\n");
     declare_stats(e);
+    const int alias_add = first_aliased_add(e);
+    if (alias_add >= 0)
+        bprintf(b, "  float2 tdbr[TKG_KCH][TKG_VP];\n"
+                   "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
+                   "    tdbr[k][q] = make_float2(0.f, 0.f);\n");
     bprintf(b, "#if TKG_STAGE_BYTES > 0\n  const int tkm_sl = tkm_it & 1;\n  tkm_cp_wait<1>();\n");
     for (int i = 0; i < nin; i++) {
         decl_array(b, rin[i].arr);
@@ -1247,6 +1276,13 @@ static void emit_plasma_bwd(Em *e) {
         emit_bwd_range(e, L->nl, L->nl + L->nr, "tgr");
         store_array(b, din, "(2 * TKG_C2)", "0", "tgl", din_acc);
         store_array(b, din, "(2 * TKG_C2)", "TKG_C2", "tgr", din_acc);
+    } else if (alias_add >= 0) {
+        /* the residual branches that feed back into the group input, summed
+         * with it; the first planned of these writes decides overwrite or
+         * accumulate */
+        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+                   "    tg[k][q].x += tdbr[k][q].x; tg[k][q].y += tdbr[k][q].y;\n  }\n");
+        store_array(b, din, "TKG_C2", "0", "tg", e->plan->add_branch_acc[alias_add] > 0);
     } else {
         store_array(b, din, "TKG_C2", "0", "tg", din_acc);
     }
