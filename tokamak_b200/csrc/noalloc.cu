@@ -15,7 +15,11 @@
 //   * rows must not exceed kMaxRows; larger calls are rejected with TKB_ERR_ARG.
 //   * The first call on a device looks up the array's device address for that
 //     device (cudaGetSymbolAddress).  Make that first call before any stream
-//     capture begins on that device.
+//     capture begins on that device; a first call made while its stream is
+//     capturing is rejected with TKB_ERR_ARG and leaves the capture intact.
+//   * The looked-up address is kept for the life of the process.  After
+//     cudaDeviceReset on a device it is stale: do not call this entry point on
+//     that device again in the same process.
 //   * All calls share the one array.  Each call writes the per-row entries it
 //     later reads, so nothing carries over between calls, but calls whose
 //     kernels overlap on the GPU (different streams, or different host
@@ -34,14 +38,24 @@ constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
 float* g_noalloc_ptr[kMaxDevices] = {nullptr};
 
-// Device address of the scratch array on the current device (looked up once per device).
-cudaError_t noalloc_scratch(float** out) {
+// Device address of the scratch array on the current device (looked up once
+// per device).  The lookup may load this library's module on the device,
+// which must not happen inside a stream capture: if the first call on a
+// device comes while `st` is capturing, *in_capture is set and nothing is
+// looked up.
+cudaError_t noalloc_scratch(float** out, cudaStream_t st, bool* in_capture) {
+  *in_capture = false;
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (!g_noalloc_ptr[dev]) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+      *in_capture = true;
+      return cudaSuccess;
+    }
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_row_loss);
     if (e != cudaSuccess) return e;
@@ -66,10 +80,15 @@ extern "C" int tkb_softmax_loss_noalloc(const void* logits, const int32_t* label
   if (rows > kNoallocMaxRows)
     return fail(TKB_ERR_ARG, "tkb_softmax_loss_noalloc: rows %d exceeds the built-in scratch limit of %d rows", rows,
                 kNoallocMaxRows);
-  float* scratch = nullptr;
-  cudaError_t e = noalloc_scratch(&scratch);
-  if (e != cudaSuccess) return cuda_status(e, "tkb_softmax_loss_noalloc: scratch address", 0);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* scratch = nullptr;
+  bool in_capture = false;
+  cudaError_t e = noalloc_scratch(&scratch, st, &in_capture);
+  if (e != cudaSuccess) return cuda_status(e, "tkb_softmax_loss_noalloc: scratch address", 0);
+  if (in_capture)
+    return fail(TKB_ERR_ARG,
+                "tkb_softmax_loss_noalloc: the first call on a device must come before any stream capture "
+                "(it looks up the scratch array's device address)");
 #define CALL(T) softmax_loss_t<T>(logits, labels, dlogits, loss, correct, scratch, rows, C, kind, gamma, st)
   return cuda_status(TKB_BY_DTYPE(dtype, CALL), "tkb_softmax_loss_noalloc", loss ? 2 : 1);
 #undef CALL
