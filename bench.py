@@ -156,7 +156,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="attention", choices=["attention", "train", "rows", "longctx", "sweep"])
+    ap.add_argument("--workload", default="attention", choices=["attention", "train", "rows", "longctx", "sweep", "gemm"])
     ap.add_argument("--seq", type=int, default=None, help="sequence length of the longctx / train workloads")
     ap.add_argument("--batch", type=int, default=None, help="sequences per GPU of the train workload")
     ap.add_argument("--profile", default=None, help="write the per-launch profile (train/rows) to this JSON file")
@@ -167,7 +167,8 @@ def main():
                     help="dtype the data-parallel gradients are averaged in")
     args = ap.parse_args()
     if args.workload != "attention":
-        return {"train": run_train, "rows": run_rows, "longctx": run_longctx, "sweep": run_sweep}[args.workload](args)
+        return {"train": run_train, "rows": run_rows, "longctx": run_longctx, "sweep": run_sweep,
+                "gemm": run_gemm}[args.workload](args)
     rank = int(os.environ.get("RANK", "0"))
 
     if args.impl == "reference":
@@ -810,6 +811,104 @@ def run_longctx(args):
     if rank == 0:
         line.update({"vs_baseline": None, "e2e": None, "cpu_baseline": None})
         print(json.dumps(line))
+    dist_done(world)
+    return 0
+
+
+# ------------------------------------------------------------ gemm (C4 GEMMs)
+
+
+GEMM_SHAPES = [
+    # (name, M, N, K, a_trans, b_trans, C fp32): one layer of configuration 4 and the LM head, 16384 tokens
+    ("qkv fwd", 16384, 3072, 2048, False, False, False),
+    ("qkv dX", 16384, 2048, 3072, False, True, False),
+    ("qkv dW", 2048, 3072, 16384, True, False, True),
+    ("o-proj fwd", 16384, 2048, 2048, False, False, False),
+    ("gate|up fwd", 16384, 11264, 2048, False, False, False),
+    ("gate|up dX", 16384, 2048, 11264, False, True, False),
+    ("gate|up dW", 2048, 11264, 16384, True, False, True),
+    ("down fwd", 16384, 2048, 5632, False, False, False),
+    ("down dX", 16384, 5632, 2048, False, True, False),
+    ("down dW", 5632, 2048, 16384, True, False, True),
+    ("lm-head fwd", 16384, 32000, 2048, False, False, False),
+]
+
+
+def run_gemm(args):
+    """The GEMMs of one configuration-4 layer and the LM head (16384 tokens)
+    on the tcgen05 kernel (tkb_gemm, and tkb_gemm_swiglu for the twin FC)
+    and on cuBLAS (torch.matmul, bf16) in the same process: TFLOP/s of each,
+    every launch timed alone with CUDA events after a 256 MB L2 flush."""
+    import torch
+
+    from tokamak_b200 import lib, ops
+    world, rank, local, dev = dist_setup()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    L = lib()
+    peak, peak_sus, hbm, src = load_peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    reps = max(5, args.steps)
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return statistics.median(ts)
+
+    n0 = L.tkb_launch_count()
+    rows = []
+    g = torch.Generator(device=dev).manual_seed(3)
+    for name, M, N, K, at, bt, f32 in GEMM_SHAPES:
+        A = (0.05 * torch.randn(*((K, M) if at else (M, K)), device=dev, generator=g)).bfloat16()
+        Bm = (0.05 * torch.randn(*((N, K) if bt else (K, N)), device=dev, generator=g)).bfloat16()
+        C = torch.empty(M, N, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
+        a_op = A.T if at else A
+        b_op = Bm.T if bt else Bm
+        ours = timed(lambda: ops.gemm(A, Bm, at, bt, out=C))
+        cublas = timed(lambda: torch.matmul(a_op, b_op))
+        fl = 2.0 * M * N * K
+        rows.append({"name": name, "M": M, "N": N, "K": K, "ms": ours, "tflops": fl / (ours * 1e-3) / 1e12,
+                     "cublas_ms": cublas, "cublas_tflops": fl / (cublas * 1e-3) / 1e12})
+        del A, Bm, C
+    # the twin FC with its SwiGLU epilogue against cuBLAS GEMM + torch SwiGLU
+    F = 5632
+    A = (0.05 * torch.randn(16384, 2048, device=dev, generator=g)).bfloat16()
+    W = (0.05 * torch.randn(2048, 2 * F, device=dev, generator=g)).bfloat16()
+    ours = timed(lambda: ops.gemm_swiglu(A, W, F))
+
+    def cublas_swiglu():
+        gu = torch.matmul(A, W)
+        return torch.nn.functional.silu(gu[:, :F]) * gu[:, F:]
+    ref = timed(cublas_swiglu)
+    fl = 2.0 * 16384 * 2 * F * 2048
+    rows.append({"name": "gate|up fwd + SwiGLU epilogue", "M": 16384, "N": 2 * F, "K": 2048, "ms": ours,
+                 "tflops": fl / (ours * 1e-3) / 1e12, "cublas_ms": ref, "cublas_tflops": fl / (ref * 1e-3) / 1e12,
+                 "cublas_path": "torch.matmul + torch SiLU*up"})
+    launches = int(L.tkb_launch_count() - n0)
+    tot_fl = sum(2.0 * r["M"] * r["N"] * r["K"] for r in rows[:-1])
+    tot_ms = sum(r["ms"] for r in rows[:-1])
+    tot_cb = sum(r["cublas_ms"] for r in rows[:-1])
+    value = tot_fl / (tot_ms * 1e-3) / 1e12
+    dom = max(rows[:-1], key=lambda r: r["ms"])
+    if rank == 0:
+        print(json.dumps({
+            "metric": "bf16 GEMM TFLOP/s (configuration-4 layer GEMMs + LM head)", "value": value,
+            "unit": "TFLOP/s", "n_gpus": world, "steps": reps, "warmup": max(3, args.warmup),
+            "ms_per_step": tot_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0, 0.05)", "config": {"workload": "gemm_c4", "l2": "256 MB flush before every launch"},
+            "cublas_tflops_same_shapes": tot_fl / (tot_cb * 1e-3) / 1e12, "kernels": rows,
+            "roofline": {"bound": "tensor", "kernel": dom["name"], "achieved": dom["tflops"], "peak": peak,
+                         "unit": "TFLOP/s", "frac": dom["tflops"] / peak,
+                         "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)", "traffic": None},
+            "e2e": None, "cpu_baseline": None, "gpu_launches": launches}))
     dist_done(world)
     return 0
 

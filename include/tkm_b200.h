@@ -188,6 +188,32 @@ typedef struct {
 int tkb_sgd_step(const tkb_sgd_tensor *table, int n_tensors, const float *lr,
                  float momentum, float weight_decay, uint32_t *seed, void *stream);
 
+/* ------------------------------------------------------------ GEMM
+ * Replaces the cuBLAS GEMMs of the FC layers (cublasGemmEx at
+ * src/tkm_gpu.cu:1207-1236 forward, 1330-1372 input and weight gradients):
+ * C[M][N] = A B (+ C when accumulate, + bias[n] when bias is not NULL),
+ * bf16 operands, fp32 accumulation on the tcgen05 tensor cores.
+ *   a_trans 0: A stored [M][K], lda elements per row; 1: A stored [K][M].
+ *   b_trans 0: B stored [K][N], ldb elements per row; 1: B stored [N][K].
+ *   c_dtype TKB_BF16 or TKB_F32 (C row-major, ldc elements per row).
+ * Forward X W: (X, 0, W, 0); input gradient dY W^T: (dY, 0, W, 1); weight
+ * gradient X^T dY: (X, 1, dY, 0).  lda and ldb must be multiples of 8, ldc
+ * of 8 (bf16) or 4 (fp32); pointers 16-byte aligned.  bias needs a_trans 0. */
+int tkb_gemm(const void *A, long long lda, int a_trans, const void *B, long long ldb, int b_trans,
+             void *C, long long ldc, int c_dtype, int accumulate, const float *bias,
+             int M, int N, int K, void *stream);
+
+/* The twin [gate | up] FC with its SwiGLU epilogue in one kernel (replaces
+ * the cuBLAS GEMM of FC_TWIN_FUSED, src/tkm_gpu.cu:1207-1236, and the twin
+ * epilogue group emitted at src/tkm_codegen.c:511-598): with [G | U] = A B,
+ * A stored [M][K], B stored [K][2F] (gate columns 0..F-1, up F..2F-1),
+ * GU[M][2F] receives [G | U] in bf16 (what the backward replays from) and
+ * H[M][F] = SiLU(G + bias_gate) * (U + bias_up), computed from the bf16 G
+ * and U.  F must be a multiple of 8; the biases may be NULL. */
+int tkb_gemm_swiglu(const void *A, long long lda, const void *B, long long ldb, int F,
+                    const float *bias_gate, const float *bias_up, void *GU, long long ldgu,
+                    void *H, long long ldh, int M, int K, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

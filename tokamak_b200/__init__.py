@@ -25,7 +25,7 @@ def lib_path():
     return os.path.join(_HERE, "libtkm_b200.so")
 
 
-_vp, _i, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t
+_vp, _i, _f, _sz, _ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_longlong
 _SIGS = {
     "tkb_version": ([], ctypes.c_char_p),
     "tkb_last_error": ([], ctypes.c_char_p),
@@ -51,6 +51,8 @@ _SIGS = {
     "tkb_softmax_loss": ([_vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _f, _i, _vp], _i),
     "tkb_softmax_loss_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp], _i),
     "tkb_sgd_step": ([_vp, _i, _vp, _f, _f, _vp, _vp], _i),
+    "tkb_gemm": ([_vp, _ll, _i, _vp, _ll, _i, _vp, _ll, _i, _i, _vp, _i, _i, _i, _vp], _i),
+    "tkb_gemm_swiglu": ([_vp, _ll, _vp, _ll, _i, _vp, _vp, _vp, _ll, _vp, _ll, _i, _i, _vp], _i),
 }
 
 

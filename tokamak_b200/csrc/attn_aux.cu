@@ -42,6 +42,23 @@ cudaError_t make_tmap_rows(CUtensorMap* m, const void* base, bool bf16, long lon
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+// 2-D tensor map over a row-major 16-bit (bf16) array of `outer` rows of `inner`
+// elements, rows `ld` elements apart; box {box_inner, box_outer}, 128-byte swizzle.
+cudaError_t make_tmap_2d(CUtensorMap* m, const void* base, long long inner, long long outer, long long ld,
+                         int box_inner, int box_outer) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16) return cudaErrorMisalignedAddress;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // Rows of the padded sequence are spread over the lanes: D/8 lanes per row
 // (one 16-byte chunk of O and of dO each), 32/(D/8) rows per warp per pass,
 // UNROLL passes with their loads issued before any reduction.

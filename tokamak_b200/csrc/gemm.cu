@@ -1,0 +1,368 @@
+// gemm.cu -- bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM +
+// TMA) with fused epilogues.
+//
+// Replaces the cuBLAS calls of the reference's FC layers (src/tkm_gpu.cu:
+// 1207-1236 forward, 1330-1372 backward): C[M][N] (+)= A[M][K] B[K][N] with
+// bf16 operands and fp32 accumulation, where each operand is stored either
+// K-contiguous or M/N-contiguous, so the forward (X W), the input gradient
+// (dY W^T) and the weight gradient (X^T dY) all run without transposes.
+//
+// Persistent kernel, one CTA per SM walking 128 x 256 output tiles (grouped
+// by eight row tiles so the resident CTAs share A and B tiles in L2):
+//   warp 0      TMA producer: 64-deep K slices of A (16 KB) and B (32 KB)
+//               into a 4-stage shared-memory ring (128-byte swizzle)
+//   warp 1      TMEM owner (512 columns = two 128 x 256 fp32 accumulators)
+//               and single-thread tcgen05.mma issuer (M=128, N=256, K=16)
+//   warps 2-5   epilogue: tcgen05.ld of one accumulator row per thread while
+//               the MMA warp fills the other accumulator, then the fused
+//               epilogue and 16-byte global stores
+// Epilogues: plain (bf16 or fp32, optionally accumulating into C), per-column
+// bias, and SwiGLU: the tile's 256 columns are 128 gate and 128 up columns
+// of the fused [gate | up] weight (B loaded from both halves), and the
+// epilogue writes [gate | up] (the backward replays from it) and
+// h = SiLU(gate + b_gate) * (up + b_up) in one pass.
+// Every wait is bounded; a timeout sets the device error word and the CTA
+// drains its copies and MMAs and frees TMEM before returning.
+#include "tkb_common.cuh"
+#include "tkb_internal.h"
+
+namespace tkb {
+
+namespace gk {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;   // 16 KB
+constexpr int B_BYTES = BN * BK * 2;   // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int NBAR = 2 * STAGES + 5;   // full[S], empty[S], acc_full[2], acc_empty[2], drain
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM = OFF_MISC + 16 + 1024;  // + slack for the 1024-byte alignment of the swizzled ring
+constexpr int GROUP_M = 8;
+enum { EPI_STORE = 0, EPI_BIAS = 1, EPI_SWIGLU = 2 };
+}  // namespace gk
+
+// Tile t -> (row tile, column tile): groups of GROUP_M row tiles; inside a
+// group consecutive tiles walk the group's row tiles for one column tile.
+TKB_DEVFN void gemm_tile(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = gk::GROUP_M * tiles_n;
+  const int g = t / per_group;
+  const int first = g * gk::GROUP_M;
+  const int gm = min(gk::GROUP_M, tiles_m - first);
+  const int r = t - g * per_group;
+  tm = first + r % gm;
+  tn = r / gm;
+}
+
+// Column of B where the i-th 64-column box of column tile tn starts.
+template <int EPI>
+TKB_DEVFN int gemm_b_col(const GemmParams& p, int tn, int i) {
+  if constexpr (EPI == gk::EPI_SWIGLU) return (i < 2 ? 0 : p.b_split) + tn * 128 + (i & 1) * 64;
+  return tn * gk::BN + i * 64;
+}
+
+TKB_DEVFN float silu_f(float x) { return x / (1.0f + ex2(-1.4426950408889634f * x)); }
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(gk::THREADS, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
+  using namespace gk;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int ntiles = p.tiles_m * p.tiles_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&p.tmA);
+      prefetch_tmap(&p.tmB);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+        int tm, tn;
+        gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
+        const int m0 = tm * BM;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
+          uint8_t* a = smem + s * STAGE_BYTES;
+          uint8_t* b = a + A_BYTES;
+          const int k0 = kb * BK;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          if constexpr (A_MN) {
+            tma_load_2d(a, &p.tmA, &full[s], m0, k0);
+            tma_load_2d(a + 8192, &p.tmA, &full[s], m0 + 64, k0);
+          } else {
+            tma_load_2d(a, &p.tmA, &full[s], k0, m0);
+          }
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) tma_load_2d(b + i * 8192, &p.tmB, &full[s], gemm_b_col<EPI>(p, tn, i), k0);
+          } else {
+            tma_load_2d(b, &p.tmB, &full[s], k0, tn * BN);
+          }
+        }
+      }
+      if (!ok) {
+        // let every copy this CTA started land before it exits
+        volatile int never = 0;
+        for (int j = max(0, it - STAGES); j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &never);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16kind(BM, BN, true, A_MN, B_MN);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x, ++tc) {
+        const int ab = tc & 1;
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!(ok = mbar_wait(&acc_empty[ab], aph ^ 1, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + ab * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!(ok = mbar_wait(&full[s], ph, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t a = sbase + s * STAGE_BYTES, b = a + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // K-major: the 16-wide K step sits 32 bytes into each 128-byte swizzled row;
+            // MN-major: it is the next two 8-row swizzle atoms (2 KB), 64-column boxes 8 KB apart
+            const uint64_t ad = A_MN ? sdesc_sw128(a + kk * 2048, 8192, 1024) : sdesc_sw128(a + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b + kk * 2048, 8192, 1024) : sdesc_sw128(b + kk * 32, 16, 1024);
+            umma_ss(d, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (ok) umma_commit(&acc_full[ab]);
+      }
+      if (!ok) {
+        // no MMA may still run when TMEM is released
+        volatile int never = 0;
+        umma_commit(drain);
+        mbar_wait(drain, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2-5)
+    const int q = warp & 3;  // TMEM lane quadrant this warp may read
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    int tc = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      int tm, tn;
+      gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int ab = tc & 1;
+      const uint32_t aph = (tc >> 1) & 1;
+      if (!mbar_wait(&acc_full[ab], aph, abort_flag)) break;
+      tc_fence_after();
+      const int row = tm * BM + q * 32 + lane;
+      const bool rv = row < p.M;
+      const uint32_t tacc = tmem + lane_off + ab * BN;
+      if constexpr (EPI == EPI_SWIGLU) {
+        const int f0 = tn * 128;
+        const int F = p.N;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tacc + c, g);
+          wait_ld_dep(g);
+          tmem_ld32(tacc + 128 + c, u);
+          wait_ld_dep(u);
+          const int col = f0 + c;
+          if (!rv || col >= F) continue;
+          uint16_t* gu_row = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc;
+          uint16_t* h_row = static_cast<uint16_t*>(p.h) + static_cast<long long>(row) * p.ldh;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {  // 8 columns per 16-byte store
+            const int c8 = col + v * 8;
+            if (c8 >= F) break;
+            float gv[8], uv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              gv[j] = __uint_as_float(g[v * 8 + j]);
+              uv[j] = __uint_as_float(u[v * 8 + j]);
+            }
+            uint32_t pg[4], pu[4], ph[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              pg[j] = pack2<true>(gv[2 * j], gv[2 * j + 1]);
+              pu[j] = pack2<true>(uv[2 * j], uv[2 * j + 1]);
+            }
+            // the twin epilogue reads the stored (bf16) gate and up values, as the unfused path does
+            float hv[8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 g2 = unpack2<true>(pg[j]), u2 = unpack2<true>(pu[j]);
+              const int n = c8 + 2 * j;
+              const float bg0 = p.bias ? p.bias[min(n, F - 1)] : 0.f, bg1 = p.bias ? p.bias[min(n + 1, F - 1)] : 0.f;
+              const float bu0 = p.bias2 ? p.bias2[min(n, F - 1)] : 0.f, bu1 = p.bias2 ? p.bias2[min(n + 1, F - 1)] : 0.f;
+              hv[2 * j] = silu_f(g2.x + bg0) * (u2.x + bu0);
+              hv[2 * j + 1] = silu_f(g2.y + bg1) * (u2.y + bu1);
+              ph[j] = pack2<true>(hv[2 * j], hv[2 * j + 1]);
+            }
+            if (c8 + 8 <= F) {
+              *reinterpret_cast<uint4*>(gu_row + c8) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
+              *reinterpret_cast<uint4*>(gu_row + p.b_split + c8) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+              *reinterpret_cast<uint4*>(h_row + c8) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (c8 + j >= F) continue;
+                const int sh = (j & 1) * 16;
+                gu_row[c8 + j] = static_cast<uint16_t>(pg[j >> 1] >> sh);
+                gu_row[p.b_split + c8 + j] = static_cast<uint16_t>(pu[j >> 1] >> sh);
+                h_row[c8 + j] = static_cast<uint16_t>(ph[j >> 1] >> sh);
+              }
+            }
+          }
+        }
+      } else {
+        const int n0 = tn * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c, r);
+          wait_ld_dep(r);
+          const int col = n0 + c;
+          if (!rv || col >= p.N) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if constexpr (EPI == EPI_BIAS) {
+            if (p.bias) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] += p.bias[min(col + j, p.N - 1)];
+            }
+          }
+          const bool whole = col + 32 <= p.N;
+          if (p.out_f32) {
+            float* dst = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+            if (whole) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                if (p.accumulate) {
+                  const float4 old = reinterpret_cast<const float4*>(dst)[j];
+                  o.x += old.x;
+                  o.y += old.y;
+                  o.z += old.z;
+                  o.w += old.w;
+                }
+                reinterpret_cast<float4*>(dst)[j] = o;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col + j < p.N) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
+            }
+          } else {
+            uint16_t* dst = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+            if (whole) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) w[e] = v[8 * j + e];
+                if (p.accumulate) {
+                  const uint4 old = reinterpret_cast<const uint4*>(dst)[j];
+                  const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 f = unpack2<true>(ow[e]);
+                    w[2 * e] += f.x;
+                    w[2 * e + 1] += f.y;
+                  }
+                }
+                reinterpret_cast<uint4*>(dst)[j] = make_uint4(pack2<true>(w[0], w[1]), pack2<true>(w[2], w[3]),
+                                                              pack2<true>(w[4], w[5]), pack2<true>(w[6], w[7]));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col + j >= p.N) continue;
+                float w = v[j];
+                if (p.accumulate) w += __uint_as_float(static_cast<uint32_t>(dst[j]) << 16);
+                dst[j] = static_cast<uint16_t>(pack2<true>(w, 0.f) & 0xFFFFu);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream) {
+  auto kern = gemm_tc_kernel<A_MN, B_MN, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gk::SMEM);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ntiles = p.tiles_m * p.tiles_n;
+  const unsigned grid = static_cast<unsigned>(min(ntiles, sms));
+  kern<<<grid, gk::THREADS, gk::SMEM, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream) {
+  if (epi == gk::EPI_SWIGLU) {
+    if (a_mn || !b_mn) return cudaErrorInvalidValue;
+    return launch_gemm<false, true, gk::EPI_SWIGLU>(p, stream);
+  }
+  if (epi == gk::EPI_BIAS) {
+    if (!a_mn && b_mn) return launch_gemm<false, true, gk::EPI_BIAS>(p, stream);
+    if (!a_mn && !b_mn) return launch_gemm<false, false, gk::EPI_BIAS>(p, stream);
+    return cudaErrorInvalidValue;
+  }
+  if (!a_mn && b_mn) return launch_gemm<false, true, gk::EPI_STORE>(p, stream);
+  if (!a_mn && !b_mn) return launch_gemm<false, false, gk::EPI_STORE>(p, stream);
+  if (a_mn && b_mn) return launch_gemm<true, true, gk::EPI_STORE>(p, stream);
+  return launch_gemm<true, false, gk::EPI_STORE>(p, stream);
+}
+
+}  // namespace tkb

@@ -4,7 +4,9 @@
 #include "attn_fwd.cu"
 #include "attn_bwd.cu"
 #include "attn_f32.cu"
+#include "gemm.cu"
 #include "rows.cu"
 #include "capi.cu"
 #include "capi_rows.cu"
+#include "capi_gemm.cu"
 #include "noalloc.cu"

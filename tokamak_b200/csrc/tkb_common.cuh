@@ -104,6 +104,15 @@ TKB_DEVFN void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int x
       : "memory");
 }
 
+// 2-D tiled load (x innermost).  x * element size must be a multiple of 16 B.
+TKB_DEVFN void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Plain bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
 TKB_DEVFN void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -40,6 +40,27 @@ struct alignas(64) BwdParams {
   float scale_log2;           // softmax scale * log2(e)
 };
 
+// GEMM parameters: C[M][N] (+)= A[M][K] B[K][N], bf16 operands, fp32 accumulation.
+// tmA / tmB are 2-D maps with 128-byte swizzle: a K-major operand (K contiguous)
+// as {K, rows} with box {64, 128 (A) or 256 (B)}; an MN-major operand (M or N
+// contiguous) as {cols, K} with box {64, 64}.
+struct alignas(64) GemmParams {
+  CUtensorMap tmA, tmB;
+  void* c;                    // C, row-major, ldc elements per row (bf16 or fp32)
+  long long ldc;
+  void* h;                    // SwiGLU: h[M][F], ldh elements per row (bf16)
+  long long ldh;
+  const float* bias;          // per-column bias of C (or the gate bias for SwiGLU); may be null
+  const float* bias2;         // SwiGLU: up bias; may be null
+  int M, N, K;                // N: columns of C (SwiGLU: F, the columns of h)
+  int tiles_m, tiles_n;
+  int b_split;                // SwiGLU: column of B where the up half starts (F)
+  int accumulate;             // C += result
+  int out_f32;                // C is fp32 (else bf16)
+};
+
+cudaError_t gemm_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream);
+
 cudaError_t attn_fwd_tc(const FwdParams& p, int D, bool bf16, cudaStream_t stream);
 cudaError_t attn_bwd_tc(const BwdParams& p, int D, bool bf16, cudaStream_t stream);
 

@@ -173,3 +173,26 @@ def sgd_table(entries, device):
 
 def sgd_step(table, n, lr_dev, momentum=0.9, wd=1e-4, seed_dev=None):
     check(lib().tkb_sgd_step(_p(table), n, _p(lr_dev), momentum, wd, _p(seed_dev), _stream()), "tkb_sgd_step")
+
+
+def gemm(A, B, a_trans=False, b_trans=False, out=None, out_dtype=None, accumulate=False, bias=None):
+    """C (+)= op(A) op(B) on the tcgen05 GEMM (tkb_gemm).  A is [M][K] (a_trans:
+    [K][M]); B is [K][N] (b_trans: [N][K]); bf16 operands, C bf16 or fp32."""
+    M = A.shape[1] if a_trans else A.shape[0]
+    K = A.shape[0] if a_trans else A.shape[1]
+    N = B.shape[0] if b_trans else B.shape[1]
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype or torch.bfloat16, device=A.device)
+    check(lib().tkb_gemm(_p(A), A.stride(0), int(a_trans), _p(B), B.stride(0), int(b_trans), _p(out), out.stride(0),
+                         dtype_code(out), int(accumulate), _p(bias), M, N, K, _stream()), "tkb_gemm")
+    return out
+
+
+def gemm_swiglu(A, B, F, bias_gate=None, bias_up=None):
+    """([G|U] bf16 [M][2F], h bf16 [M][F]) with [G|U] = A B and h = SiLU(G + b_g) * (U + b_u)."""
+    M, K = A.shape
+    gu = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=A.device)
+    h = torch.empty(M, F, dtype=torch.bfloat16, device=A.device)
+    check(lib().tkb_gemm_swiglu(_p(A), A.stride(0), _p(B), B.stride(0), F, _p(bias_gate), _p(bias_up), _p(gu),
+                                gu.stride(0), _p(h), h.stride(0), M, K, _stream()), "tkb_gemm_swiglu")
+    return gu, h
