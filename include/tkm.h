@@ -335,6 +335,25 @@ TKM_API int tkm_runtime_init_weights(TkmRuntime *rt, unsigned long long seed, fl
  * their own work against it. */
 TKM_API void *tkm_runtime_stream(const TkmRuntime *rt);
 
+/* Datasets beyond the reference's uint8 per-sample labels, for
+ * tkm_runtime_train_epoch.  Like tkm_dataset_create they live on the device
+ * when they fit in half the free device memory (tkm_dataset_is_resident);
+ * an epoch then gathers every batch on the device inside one captured graph
+ * per step and reads the loss back once.
+ *   _i32:    h_inputs as tkm_dataset_create, and one int32 label per loss
+ *            row: [num_samples][loss rows per sample] (sequence models,
+ *            vocabularies above 256).
+ *   _tokens: token sequences h_tokens [num_seqs][S + 1] (S = the input's
+ *            rows per sample) over an embedding table h_embed [vocab][C]
+ *            (C = the input's channels): input row p of a sequence is
+ *            h_embed[token p], its label is token p + 1.  Needs one loss row
+ *            per input row.
+ * Labels and tokens are checked against the loss width and the table. */
+TKM_API TkmDataset *tkm_dataset_create_i32(TkmRuntime *rt, const float *h_inputs, const int32_t *h_labels,
+                                           size_t num_samples);
+TKM_API TkmDataset *tkm_dataset_create_tokens(TkmRuntime *rt, const float *h_embed, int vocab,
+                                              const int32_t *h_tokens, size_t num_seqs);
+
 #ifdef __cplusplus
 }
 #endif

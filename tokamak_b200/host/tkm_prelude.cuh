@@ -479,6 +479,73 @@ extern "C" __global__ void __launch_bounds__(256) tkm_bf16_to_f32(const uint16_t
     dst[i] = __uint_as_float((uint32_t)src[i] << 16);
 }
 
+// ------------------------------------------- device-resident datasets
+// One batch of a resident dataset: sample i of batch b is sample order[b*B + i]
+// (b read from *batch).  Its `per` input values (activation storage) are copied
+// by blockIdx.y-strided 16-byte chunks when they allow it, and its
+// labels_per_sample int32 labels follow.  Grid (B, chunks).
+extern "C" __global__ void __launch_bounds__(256) tkm_ds_gather(const tkm_act_t* __restrict__ src,
+                                                                const int* __restrict__ labels,
+                                                                const unsigned* __restrict__ order,
+                                                                const unsigned* __restrict__ batch,
+                                                                tkm_act_t* __restrict__ dst, int* __restrict__ dlabels,
+                                                                long long per, int labels_per_sample, int B) {
+  const int i = blockIdx.x;
+  const unsigned s = order[(size_t)(*batch) * B + i];
+  const tkm_act_t* in = src + (size_t)s * per;
+  tkm_act_t* out = dst + (size_t)i * per;
+  const int vec = 16 / (int)sizeof(tkm_act_t);
+  if (per % vec == 0) {
+    const long long nv = per / vec;
+    for (long long k = blockIdx.y * 256ll + threadIdx.x; k < nv; k += (long long)gridDim.y * 256)
+      reinterpret_cast<uint4*>(out)[k] = reinterpret_cast<const uint4*>(in)[k];
+  } else {
+    for (long long k = blockIdx.y * 256ll + threadIdx.x; k < per; k += (long long)gridDim.y * 256) out[k] = in[k];
+  }
+  if (blockIdx.y == 0)
+    for (int k = threadIdx.x; k < labels_per_sample; k += 256)
+      dlabels[(size_t)i * labels_per_sample + k] = labels[(size_t)s * labels_per_sample + k];
+}
+
+// One batch of token sequences: sequence i of batch b is order[b*B + i] in
+// tokens[n][S+1]; input row (i, p) is the embedding row table[tokens[p]]
+// (activation storage, C values) and its label is tokens[p+1].  Grid (B, S).
+extern "C" __global__ void __launch_bounds__(256) tkm_ds_tokens(const tkm_act_t* __restrict__ table,
+                                                                const int* __restrict__ tokens,
+                                                                const unsigned* __restrict__ order,
+                                                                const unsigned* __restrict__ batch,
+                                                                tkm_act_t* __restrict__ dst, int* __restrict__ dlabels,
+                                                                int S, int C, int B) {
+  const int i = blockIdx.x, p = blockIdx.y;
+  const unsigned s = order[(size_t)(*batch) * B + i];
+  const int* seq = tokens + (size_t)s * (S + 1);
+  const int tok = seq[p];
+  const tkm_act_t* in = table + (size_t)tok * C;
+  tkm_act_t* out = dst + ((size_t)i * S + p) * C;
+  const int vec = 16 / (int)sizeof(tkm_act_t);
+  if (C % vec == 0) {
+    for (int k = threadIdx.x; k < C / vec; k += 256) reinterpret_cast<uint4*>(out)[k] = reinterpret_cast<const uint4*>(in)[k];
+  } else {
+    for (int k = threadIdx.x; k < C; k += 256) out[k] = in[k];
+  }
+  if (threadIdx.x == 0) dlabels[(size_t)i * S + p] = seq[p + 1];
+}
+
+// Learning rate of the step about to run: lr_table[*batch].
+extern "C" __global__ void tkm_ds_lr(const float* __restrict__ lr_table, const unsigned* __restrict__ batch,
+                                     float* __restrict__ lr) {
+  if (threadIdx.x == 0) *lr = lr_table[*batch];
+}
+
+// After a step: the epoch's loss sum grows by the step's loss; next batch.
+extern "C" __global__ void tkm_ds_end(const float* __restrict__ loss, float* __restrict__ loss_sum,
+                                      unsigned* __restrict__ batch) {
+  if (threadIdx.x == 0) {
+    *loss_sum += *loss;
+    *batch += 1u;
+  }
+}
+
 // uint8 class labels (one per sample, the reference's format) -> int32 per row
 extern "C" __global__ void __launch_bounds__(256) tkm_labels_u8(const uint8_t* __restrict__ src, int n_src,
                                                                 int* __restrict__ dst, int rows) {

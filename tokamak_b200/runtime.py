@@ -55,6 +55,12 @@ _SIGS = {
     "tkm_runtime_init_weights": ([_vp, _c.c_ulonglong, _f], _i),
     "tkm_runtime_stream": ([_vp], _vp),
     "tkm_runtime_optimizer_bytes": ([_vp], _sz),
+    "tkm_dataset_create": ([_vp, _vp, _vp, _sz], _vp),
+    "tkm_dataset_create_i32": ([_vp, _vp, _vp, _sz], _vp),
+    "tkm_dataset_create_tokens": ([_vp, _vp, _i, _vp, _sz], _vp),
+    "tkm_dataset_free": ([_vp], None),
+    "tkm_dataset_is_resident": ([_vp], _i),
+    "tkm_runtime_train_epoch": ([_vp, _vp, _vp, _f, _f, _sz, _sz, _sz, _c.POINTER(_f)], _i),
     "tkm_save_optimizer_buffer": ([_vp, _vp, _sz, _c.POINTER(_sz)], _i),
     "tkm_load_optimizer_buffer": ([_vp, _vp, _sz], _i),
 }
@@ -108,7 +114,9 @@ class Runtime:
 
     @classmethod
     def from_dsl(cls, text, batch, dtype=DTYPE_BF16):
-        return cls(lib().tkm_load_string_ex(text.encode(), int(batch), int(dtype)))
+        rt = cls(lib().tkm_load_string_ex(text.encode(), int(batch), int(dtype)))
+        rt.batch = int(batch)
+        return rt
 
     @classmethod
     def from_file(cls, path, batch):
@@ -259,6 +267,59 @@ class Runtime:
         if not n:
             raise TkbError("dp_allreduce_time: " + last_error())
         return float(ms.value), int(n)
+
+
+class Dataset:
+    """A training dataset of the engine (tkm_dataset_create*).  Keeps the
+    host arrays alive for its lifetime (the engine copies them)."""
+
+    def __init__(self, rt, inputs, labels=None, tokens=None, embed=None):
+        L = lib()
+        self.rt = rt
+        if tokens is not None:
+            self._keep = (np.ascontiguousarray(embed, np.float32), np.ascontiguousarray(tokens, np.int32))
+            h = L.tkm_dataset_create_tokens(rt.h, _ptr(self._keep[0]), int(self._keep[0].shape[0]),
+                                            _ptr(self._keep[1]), int(self._keep[1].shape[0]))
+        else:
+            x = np.ascontiguousarray(inputs, np.float32)
+            n = int(x.size // (rt.input_elements // self._batch(rt)))
+            if np.asarray(labels).dtype == np.uint8:
+                y = np.ascontiguousarray(labels, np.uint8)
+                h = L.tkm_dataset_create(rt.h, _ptr(x), _ptr(y), n)
+            else:
+                y = np.ascontiguousarray(labels, np.int32)
+                h = L.tkm_dataset_create_i32(rt.h, _ptr(x), _ptr(y), n)
+            self._keep = (x, y)
+        if not h:
+            raise TkbError("dataset creation failed: " + last_error())
+        self.h = _vp(h)
+
+    @staticmethod
+    def _batch(rt):
+        return rt.batch
+
+    @property
+    def resident(self):
+        return bool(lib().tkm_dataset_is_resident(self.h))
+
+    def train_epoch(self, order=None, peak_lr=0.01, min_lr_ratio=0.1, step0=0, total_steps=100, warmup=0):
+        o = None if order is None else np.ascontiguousarray(order, np.uint32)
+        avg = _f(0.0)
+        if not lib().tkm_runtime_train_epoch(self.rt.h, self.h, _ptr(o), float(peak_lr), float(min_lr_ratio),
+                                             int(step0), int(total_steps), int(warmup), ctypes.byref(avg)):
+            raise TkbError("train_epoch: " + last_error())
+        return float(avg.value)
+
+    def close(self):
+        if self.h:
+            lib().tkm_dataset_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def plan_buckets(sizes, nodes, has_grad, target_elems, cap=64):
