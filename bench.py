@@ -165,7 +165,12 @@ def main():
     ap.add_argument("--train-steps", type=int, default=10, help="timed steps of the train object")
     ap.add_argument("--dp-grad-dtype", default="bf16", choices=["bf16", "fp32"],
                     help="dtype the data-parallel gradients are averaged in")
+    ap.add_argument("--gemm-shape", default=None, help="gemm workload: run only the shape with this name")
+    ap.add_argument("--gemm", default=None, choices=["cublas", "tc"],
+                    help="the engine's FC GEMMs: cuBLAS (default) or the tcgen05 kernel (sets TKM_GEMM)")
     args = ap.parse_args()
+    if args.gemm:
+        os.environ["TKM_GEMM"] = args.gemm
     if args.workload != "attention":
         return {"train": run_train, "rows": run_rows, "longctx": run_longctx, "sweep": run_sweep,
                 "gemm": run_gemm}[args.workload](args)
@@ -589,8 +594,9 @@ def measure_train(args, world, rank, local, dev, cfg, steps, warmup):
                    "ffn": F, "vocab": V, "seq_len": T, "micro_batch": B_, "global_batch": B_ * world,
                    "parallelism": f"dp{world}", "graph": "whole step captured as one CUDA graph",
                    "grad_allreduce_dtype": args.dp_grad_dtype if world > 1 else None,
+                   "gemm": "tcgen05 kernel" if os.environ.get("TKM_GEMM") == "tc" else "cuBLAS",
                    "l2": "working set far above L2 (activations ~40 GB)"},
-        "ignite_s": ignite_s, "loss_first_step": first, "loss_last": last,
+        "ignite_s": ignite_s, "loss_first_step": first, "loss_last": last, "host_cpus": host_cpus(),
         "dp_weights_identical_across_ranks": len(set(digests)) == 1, "weights_sha256": digests[0][:16],
         "allreduce": allreduce,
         "roofline": {"bound": "tensor", "kernel": "whole step (GEMM + attention FLOPs)", "achieved": achieved,
@@ -609,6 +615,22 @@ def measure_train(args, world, rank, local, dev, cfg, steps, warmup):
         rec["profile_ms_by_kind"] = by_kind
         rec["gpu_launches"] = len(prof)
     return rec
+
+
+def host_cpus():
+    """CPUs this process may use and the container's CPU quota (cgroup v2
+    cpu.max), recorded beside the end-to-end numbers they can limit."""
+    out = {"os_cpus": os.cpu_count()}
+    try:
+        out["affinity"] = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        pass
+    try:
+        with open("/sys/fs/cgroup/cpu.max") as f:
+            out["cgroup_cpu_max"] = f.read().strip()
+    except OSError:
+        pass
+    return out
 
 
 def run_train(args):
@@ -867,6 +889,8 @@ def run_gemm(args):
     rows = []
     g = torch.Generator(device=dev).manual_seed(3)
     for name, M, N, K, at, bt, f32 in GEMM_SHAPES:
+        if args.gemm_shape and name != args.gemm_shape:
+            continue
         A = (0.05 * torch.randn(*((K, M) if at else (M, K)), device=dev, generator=g)).bfloat16()
         Bm = (0.05 * torch.randn(*((N, K) if bt else (K, N)), device=dev, generator=g)).bfloat16()
         C = torch.empty(M, N, dtype=torch.float32 if f32 else torch.bfloat16, device=dev)
@@ -878,6 +902,12 @@ def run_gemm(args):
         rows.append({"name": name, "M": M, "N": N, "K": K, "ms": ours, "tflops": fl / (ours * 1e-3) / 1e12,
                      "cublas_ms": cublas, "cublas_tflops": fl / (cublas * 1e-3) / 1e12})
         del A, Bm, C
+    if args.gemm_shape:
+        if rank == 0:
+            print(json.dumps({"metric": "bf16 GEMM TFLOP/s (one shape)", "kernels": rows,
+                              "gpu_launches": int(L.tkb_launch_count() - n0)}))
+        dist_done(world)
+        return 0
     # the twin FC with its SwiGLU epilogue against cuBLAS GEMM + torch SwiGLU
     F = 5632
     A = (0.05 * torch.randn(16384, 2048, device=dev, generator=g)).bfloat16()

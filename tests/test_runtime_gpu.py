@@ -365,3 +365,17 @@ def test_residual_whose_skip_is_the_group_input(dtype_name):
     tols = (1e-4, 1e-4, 1e-4) if dtype_name == "F32" else (1e-2, 2e-2, 2e-2)
     rt, *_ = compare_step(DSL["residual_of_input"], 8, dtype, np.random.default_rng(31), *tols)
     rt.close()
+
+
+@pytest.mark.parametrize("batch", [4, 64], ids=["c1", "8192_rows"])
+def test_engine_step_on_the_tcgen05_gemm(monkeypatch, batch):
+    """The configuration-1 model (one layer at 8192 rows, or both layers at
+    512) with its FC GEMMs -- forward, input gradient and weight gradient --
+    on libtkm_b200's tcgen05 kernel (TKM_GEMM=tc) instead of cuBLAS."""
+    from tokamak_b200.configs import C1, dsl_for
+    monkeypatch.setenv("TKM_GEMM", "tc")
+    rt_mod = runtime_mod()
+    cfg = dict(C1, layers=1, batch=batch) if batch > 4 else C1
+    rt, *_ = compare_step(dsl_for(cfg), cfg["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(40 + batch),
+                          1e-2, 2e-2, 5e-2)
+    rt.close()
