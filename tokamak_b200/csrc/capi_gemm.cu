@@ -1,5 +1,7 @@
 // capi_gemm.cu -- extern "C" GEMM entry points of include/tkm_b200.h:
 // argument checks, the two tensor maps and the launch of gemm.cu's kernel.
+#include <cstdlib>
+
 #include "tkb_common.cuh"
 #include "tkb_internal.h"
 #include "../../include/tkm_b200.h"
@@ -10,6 +12,15 @@ cudaError_t make_tmap_2d(CUtensorMap* m, const void* base, long long inner, long
 }
 
 namespace {
+
+// CTA-pair kernels unless TKB_GEMM_PAIR=0 (read once per process).
+bool use_pairs() {
+  static const bool v = [] {
+    const char* e = getenv("TKB_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return v;
+}
 
 // A K-major operand (K contiguous) is loaded as {64 K, rows} boxes; an
 // MN-major one as {64 columns, 64 K} boxes.
@@ -36,9 +47,10 @@ int tkb_gemm(const void* A, long long lda, int a_trans, const void* B, long long
     return fail(TKB_ERR_ARG, "tkb_gemm: ldc (%lld) must be >= N and a multiple of %d", ldc, c_dtype == TKB_F32 ? 4 : 8);
   tkb::GemmParams p{};
   const bool a_mn = a_trans != 0, b_mn = b_trans == 0;  // B stored [K][N] is N-contiguous
+  const bool pair = use_pairs();
   int rc = gemm_operand_map(&p.tmA, A, lda, a_mn, M, K, 128, "A");
   if (rc) return rc;
-  rc = gemm_operand_map(&p.tmB, B, ldb, b_mn, N, K, 256, "B");
+  rc = gemm_operand_map(&p.tmB, B, ldb, b_mn, N, K, pair ? 128 : 256, "B");
   if (rc) return rc;
   p.c = C;
   p.ldc = ldc;
@@ -46,13 +58,15 @@ int tkb_gemm(const void* A, long long lda, int a_trans, const void* B, long long
   p.M = M;
   p.N = N;
   p.K = K;
-  p.tiles_m = (M + 127) / 128;
+  p.tiles_m = pair ? (M + 255) / 256 : (M + 127) / 128;
   p.tiles_n = (N + 255) / 256;
   p.accumulate = accumulate != 0;
   p.out_f32 = c_dtype == TKB_F32;
   const int epi = bias ? 1 : 0;
   if (bias && a_mn) return fail(TKB_ERR_UNSUPPORTED, "tkb_gemm: bias with A stored [K][M]");
-  return cuda_status(tkb::gemm_tc(p, a_mn, b_mn, epi, static_cast<cudaStream_t>(stream)), "tkb_gemm", 1);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return cuda_status(pair ? tkb::gemm_pair_tc(p, a_mn, b_mn, epi, st) : tkb::gemm_tc(p, a_mn, b_mn, epi, st),
+                     "tkb_gemm", 1);
 }
 
 int tkb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, int F, const float* bias_gate,
@@ -78,10 +92,13 @@ int tkb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, 
   p.M = M;
   p.N = F;
   p.K = K;
-  p.tiles_m = (M + 127) / 128;
+  const bool pair = use_pairs();
+  p.tiles_m = pair ? (M + 255) / 256 : (M + 127) / 128;
   p.tiles_n = (F + 127) / 128;
   p.b_split = F;
-  return cuda_status(tkb::gemm_tc(p, false, true, 2, static_cast<cudaStream_t>(stream)), "tkb_gemm_swiglu", 1);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return cuda_status(pair ? tkb::gemm_pair_tc(p, false, true, 2, st) : tkb::gemm_tc(p, false, true, 2, st),
+                     "tkb_gemm_swiglu", 1);
 }
 
 }  // extern "C"

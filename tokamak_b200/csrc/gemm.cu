@@ -62,6 +62,144 @@ TKB_DEVFN int gemm_b_col(const GemmParams& p, int tn, int i) {
 
 TKB_DEVFN float silu_f(float x) { return x / (1.0f + ex2(-1.4426950408889634f * x)); }
 
+// The epilogue of one accumulator tile for this thread's row: TMEM columns
+// 0..255 of the accumulator at `tacc` (this warp's lane quadrant) -> C (and H).
+template <int EPI>
+TKB_DEVFN void gemm_epilogue(const GemmParams& p, uint32_t tacc, int row, int tn) {
+  using namespace gk;
+  const bool rv = row < p.M;
+  if constexpr (EPI == EPI_SWIGLU) {
+    const int f0 = tn * 128;
+    const int F = p.N;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tacc + c, g);
+      wait_ld_dep(g);
+      tmem_ld32(tacc + 128 + c, u);
+      wait_ld_dep(u);
+      const int col = f0 + c;
+      if (!rv || col >= F) continue;
+      uint16_t* gu_row = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc;
+      uint16_t* h_row = static_cast<uint16_t*>(p.h) + static_cast<long long>(row) * p.ldh;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {  // 8 columns per 16-byte store
+        const int c8 = col + v * 8;
+        if (c8 >= F) break;
+        float gv[8], uv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          gv[j] = __uint_as_float(g[v * 8 + j]);
+          uv[j] = __uint_as_float(u[v * 8 + j]);
+        }
+        uint32_t pg[4], pu[4], ph[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          pg[j] = pack2<true>(gv[2 * j], gv[2 * j + 1]);
+          pu[j] = pack2<true>(uv[2 * j], uv[2 * j + 1]);
+        }
+        // the twin epilogue reads the stored (bf16) gate and up values, as the unfused path does
+        float hv[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 g2 = unpack2<true>(pg[j]), u2 = unpack2<true>(pu[j]);
+          const int n = c8 + 2 * j;
+          const float bg0 = p.bias ? p.bias[min(n, F - 1)] : 0.f, bg1 = p.bias ? p.bias[min(n + 1, F - 1)] : 0.f;
+          const float bu0 = p.bias2 ? p.bias2[min(n, F - 1)] : 0.f, bu1 = p.bias2 ? p.bias2[min(n + 1, F - 1)] : 0.f;
+          hv[2 * j] = silu_f(g2.x + bg0) * (u2.x + bu0);
+          hv[2 * j + 1] = silu_f(g2.y + bg1) * (u2.y + bu1);
+          ph[j] = pack2<true>(hv[2 * j], hv[2 * j + 1]);
+        }
+        if (c8 + 8 <= F) {
+          *reinterpret_cast<uint4*>(gu_row + c8) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
+          *reinterpret_cast<uint4*>(gu_row + p.b_split + c8) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
+          *reinterpret_cast<uint4*>(h_row + c8) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (c8 + j >= F) continue;
+            const int sh = (j & 1) * 16;
+            gu_row[c8 + j] = static_cast<uint16_t>(pg[j >> 1] >> sh);
+            gu_row[p.b_split + c8 + j] = static_cast<uint16_t>(pu[j >> 1] >> sh);
+            h_row[c8 + j] = static_cast<uint16_t>(ph[j >> 1] >> sh);
+          }
+        }
+      }
+    }
+  } else {
+    const int n0 = tn * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tacc + c, r);
+      wait_ld_dep(r);
+      const int col = n0 + c;
+      if (!rv || col >= p.N) continue;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      if constexpr (EPI == EPI_BIAS) {
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] += p.bias[min(col + j, p.N - 1)];
+        }
+      }
+      const bool whole = col + 32 <= p.N;
+      if (p.out_f32) {
+        float* dst = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+        if (whole) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (p.accumulate) {
+              const float4 old = reinterpret_cast<const float4*>(dst)[j];
+              o.x += old.x;
+              o.y += old.y;
+              o.z += old.z;
+              o.w += old.w;
+            }
+            reinterpret_cast<float4*>(dst)[j] = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col + j < p.N) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
+        }
+      } else {
+        uint16_t* dst = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+        if (whole) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) w[e] = v[8 * j + e];
+            if (p.accumulate) {
+              const uint4 old = reinterpret_cast<const uint4*>(dst)[j];
+              const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<true>(ow[e]);
+                w[2 * e] += f.x;
+                w[2 * e + 1] += f.y;
+              }
+            }
+            reinterpret_cast<uint4*>(dst)[j] = make_uint4(pack2<true>(w[0], w[1]), pack2<true>(w[2], w[3]),
+                                                          pack2<true>(w[4], w[5]), pack2<true>(w[6], w[7]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col + j >= p.N) continue;
+            float w = v[j];
+            if (p.accumulate) w += __uint_as_float(static_cast<uint32_t>(dst[j]) << 16);
+            dst[j] = static_cast<uint16_t>(pack2<true>(w, 0.f) & 0xFFFFu);
+          }
+        }
+      }
+    }
+  }
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(gk::THREADS, 1) gemm_tc_kernel(const __grid_constant__ GemmParams p) {
   using namespace gk;
@@ -191,138 +329,7 @@ __global__ void __launch_bounds__(gk::THREADS, 1) gemm_tc_kernel(const __grid_co
       if (!mbar_wait(&acc_full[ab], aph, abort_flag)) break;
       tc_fence_after();
       const int row = tm * BM + q * 32 + lane;
-      const bool rv = row < p.M;
-      const uint32_t tacc = tmem + lane_off + ab * BN;
-      if constexpr (EPI == EPI_SWIGLU) {
-        const int f0 = tn * 128;
-        const int F = p.N;
-#pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tacc + c, g);
-          wait_ld_dep(g);
-          tmem_ld32(tacc + 128 + c, u);
-          wait_ld_dep(u);
-          const int col = f0 + c;
-          if (!rv || col >= F) continue;
-          uint16_t* gu_row = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc;
-          uint16_t* h_row = static_cast<uint16_t*>(p.h) + static_cast<long long>(row) * p.ldh;
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {  // 8 columns per 16-byte store
-            const int c8 = col + v * 8;
-            if (c8 >= F) break;
-            float gv[8], uv[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              gv[j] = __uint_as_float(g[v * 8 + j]);
-              uv[j] = __uint_as_float(u[v * 8 + j]);
-            }
-            uint32_t pg[4], pu[4], ph[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              pg[j] = pack2<true>(gv[2 * j], gv[2 * j + 1]);
-              pu[j] = pack2<true>(uv[2 * j], uv[2 * j + 1]);
-            }
-            // the twin epilogue reads the stored (bf16) gate and up values, as the unfused path does
-            float hv[8];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float2 g2 = unpack2<true>(pg[j]), u2 = unpack2<true>(pu[j]);
-              const int n = c8 + 2 * j;
-              const float bg0 = p.bias ? p.bias[min(n, F - 1)] : 0.f, bg1 = p.bias ? p.bias[min(n + 1, F - 1)] : 0.f;
-              const float bu0 = p.bias2 ? p.bias2[min(n, F - 1)] : 0.f, bu1 = p.bias2 ? p.bias2[min(n + 1, F - 1)] : 0.f;
-              hv[2 * j] = silu_f(g2.x + bg0) * (u2.x + bu0);
-              hv[2 * j + 1] = silu_f(g2.y + bg1) * (u2.y + bu1);
-              ph[j] = pack2<true>(hv[2 * j], hv[2 * j + 1]);
-            }
-            if (c8 + 8 <= F) {
-              *reinterpret_cast<uint4*>(gu_row + c8) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
-              *reinterpret_cast<uint4*>(gu_row + p.b_split + c8) = make_uint4(pu[0], pu[1], pu[2], pu[3]);
-              *reinterpret_cast<uint4*>(h_row + c8) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (c8 + j >= F) continue;
-                const int sh = (j & 1) * 16;
-                gu_row[c8 + j] = static_cast<uint16_t>(pg[j >> 1] >> sh);
-                gu_row[p.b_split + c8 + j] = static_cast<uint16_t>(pu[j >> 1] >> sh);
-                h_row[c8 + j] = static_cast<uint16_t>(ph[j >> 1] >> sh);
-              }
-            }
-          }
-        }
-      } else {
-        const int n0 = tn * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tacc + c, r);
-          wait_ld_dep(r);
-          const int col = n0 + c;
-          if (!rv || col >= p.N) continue;
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-          if constexpr (EPI == EPI_BIAS) {
-            if (p.bias) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += p.bias[min(col + j, p.N - 1)];
-            }
-          }
-          const bool whole = col + 32 <= p.N;
-          if (p.out_f32) {
-            float* dst = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc + col;
-            if (whole) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                if (p.accumulate) {
-                  const float4 old = reinterpret_cast<const float4*>(dst)[j];
-                  o.x += old.x;
-                  o.y += old.y;
-                  o.z += old.z;
-                  o.w += old.w;
-                }
-                reinterpret_cast<float4*>(dst)[j] = o;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col + j < p.N) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
-            }
-          } else {
-            uint16_t* dst = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc + col;
-            if (whole) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                float w[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) w[e] = v[8 * j + e];
-                if (p.accumulate) {
-                  const uint4 old = reinterpret_cast<const uint4*>(dst)[j];
-                  const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const float2 f = unpack2<true>(ow[e]);
-                    w[2 * e] += f.x;
-                    w[2 * e + 1] += f.y;
-                  }
-                }
-                reinterpret_cast<uint4*>(dst)[j] = make_uint4(pack2<true>(w[0], w[1]), pack2<true>(w[2], w[3]),
-                                                              pack2<true>(w[4], w[5]), pack2<true>(w[6], w[7]));
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (col + j >= p.N) continue;
-                float w = v[j];
-                if (p.accumulate) w += __uint_as_float(static_cast<uint32_t>(dst[j]) << 16);
-                dst[j] = static_cast<uint16_t>(pack2<true>(w, 0.f) & 0xFFFFu);
-              }
-            }
-          }
-        }
-      }
+      gemm_epilogue<EPI>(p, tmem + lane_off + ab * BN, row, tn);
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);
     }
@@ -336,6 +343,219 @@ __global__ void __launch_bounds__(gk::THREADS, 1) gemm_tc_kernel(const __grid_co
   }
 }
 
+// ----------------------------------------------------------------------------
+// CTA-pair form (tcgen05.mma.cta_group::2): a cluster of two CTAs on the two
+// SMs of a TPC computes a 256 x 256 tile.  Each CTA loads its own 128 rows of
+// A and its own 128 columns of B (32 KB per 64-deep stage instead of 48 KB),
+// so the 6-stage 192 KB ring covers twice the load latency of the one-CTA
+// form; the leader's single MMA thread issues M=256 x N=256 MMAs that read
+// both CTAs' shared memory, and each CTA's TMEM holds its 128 rows x 256
+// columns (two accumulators, 512 columns).  Barriers:
+//   full[s]      leader only: armed by the leader with both CTAs' bytes, the
+//                peer's copies complete on it remotely;
+//   empty[s]     per CTA: the leader's commit arrives on both;
+//   acc_full[a]  per CTA: the leader's commit arrives on both;
+//   acc_empty[a] leader only: one arrival per epilogue warp of both CTAs.
+// No load is multicast.
+namespace gk2 {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6, THREADS = 192;
+constexpr int A_BYTES = BM * BK * 2;         // 16 KB
+constexpr int B_BYTES = (BN / 2) * BK * 2;   // 16 KB: this CTA's half of B
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+constexpr int NBAR = 2 * STAGES + 5;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM = OFF_MISC + 16 + 1024;
+}  // namespace gk2
+
+template <int EPI>
+TKB_DEVFN int gemm_pair_b_col(const GemmParams& p, int tn, uint32_t rank) {
+  if constexpr (EPI == gk::EPI_SWIGLU) return (rank ? p.b_split : 0) + tn * 128;
+  return tn * gk2::BN + static_cast<int>(rank) * 128;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+  using namespace gk2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
+
+  const int warp = warp_id(), lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = static_cast<int>(blockIdx.x >> 1), nclusters = static_cast<int>(gridDim.x >> 1);
+  const int ntiles = p.tiles_m * p.tiles_n;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised and TMEM allocated before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      prefetch_tmap(&p.tmA);
+      prefetch_tmap(&p.tmB);
+      const uint32_t full0_leader = mapa_shared(smem_u32(&full[0]), 0);
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster; ok && t < ntiles; t += nclusters) {
+        int tm, tn;
+        gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
+        const int m0 = tm * 256 + static_cast<int>(rank) * BM;
+        const int nb = gemm_pair_b_col<EPI>(p, tn, rank);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
+          uint8_t* a = smem + s * STAGE_BYTES;
+          uint8_t* b = a + A_BYTES;
+          const int k0 = kb * BK;
+          const uint32_t bar = full0_leader + static_cast<uint32_t>(s) * 8u;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+          if constexpr (A_MN) {
+            tma_load_2d_pair(a, &p.tmA, bar, m0, k0);
+            tma_load_2d_pair(a + 8192, &p.tmA, bar, m0 + 64, k0);
+          } else {
+            tma_load_2d_pair(a, &p.tmA, bar, k0, m0);
+          }
+          if constexpr (B_MN) {
+            tma_load_2d_pair(b, &p.tmB, bar, nb, k0);
+            tma_load_2d_pair(b + 8192, &p.tmB, bar, nb + 64, k0);
+          } else {
+            tma_load_2d_pair(b, &p.tmB, bar, k0, nb);
+          }
+        }
+      }
+      if (!ok) {
+        // let the copies in flight land before the CTA leaves: the leader
+        // waits for the stages it armed (they count both CTAs' bytes), the
+        // peer gives its own copies a fixed time
+        volatile int never = 0;
+        if (leader) {
+          for (int j = max(0, it - STAGES); j < it; ++j)
+            mbar_wait_cluster(&full[j % STAGES], (j / STAGES) & 1, &never);
+        } else {
+          const unsigned long long t0 = globaltimer();
+          while (globaltimer() - t0 < 200000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_f16kind(2 * BM, BN, true, A_MN, B_MN);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int t = cluster; ok && t < ntiles; t += nclusters, ++tc) {
+        const int ab = tc & 1;
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!(ok = mbar_wait_cluster(&acc_empty[ab], aph ^ 1, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + ab * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!(ok = mbar_wait_cluster(&full[s], ph, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t a = sbase + s * STAGE_BYTES, b = a + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a + kk * 2048, 8192, 1024) : sdesc_sw128(a + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b + kk * 2048, 8192, 1024) : sdesc_sw128(b + kk * 32, 16, 1024);
+            umma_pair_ss(d, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+          }
+          umma_pair_commit(&empty[s], 0x3);  // both CTAs' stage s is free once these MMAs read it
+        }
+        if (ok) umma_pair_commit(&acc_full[ab], 0x3);
+      }
+      if (!ok) {
+        volatile int never = 0;
+        umma_pair_commit(drain, 0x1);
+        mbar_wait(drain, 0, &never);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2-5, both CTAs)
+    const int q = warp & 3;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int tc = 0;
+    for (int t = cluster; t < ntiles; t += nclusters, ++tc) {
+      int tm, tn;
+      gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int ab = tc & 1;
+      const uint32_t aph = (tc >> 1) & 1;
+      if (!mbar_wait(&acc_full[ab], aph, abort_flag)) break;
+      tc_fence_after();
+      const int row = tm * 256 + static_cast<int>(rank) * BM + q * 32 + lane;
+      gemm_epilogue<EPI>(p, tmem + lane_off + ab * BN, row, tn);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_leader + static_cast<uint32_t>(ab) * 8u);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other may still signal it or read its shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static cudaError_t launch_gemm_pair(const GemmParams& p, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gk2::SMEM);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ntiles = p.tiles_m * p.tiles_n;
+  const int nclusters = min(ntiles, sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * nclusters));
+  cfg.blockDim = dim3(gk2::THREADS);
+  cfg.dynamicSmemBytes = gk2::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 static cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream) {
   auto kern = gemm_tc_kernel<A_MN, B_MN, EPI>;
@@ -347,6 +567,22 @@ static cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream) {
   const unsigned grid = static_cast<unsigned>(min(ntiles, sms));
   kern<<<grid, gk::THREADS, gk::SMEM, stream>>>(p);
   return cudaGetLastError();
+}
+
+cudaError_t gemm_pair_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream) {
+  if (epi == gk::EPI_SWIGLU) {
+    if (a_mn || !b_mn) return cudaErrorInvalidValue;
+    return launch_gemm_pair<false, true, gk::EPI_SWIGLU>(p, stream);
+  }
+  if (epi == gk::EPI_BIAS) {
+    if (!a_mn && b_mn) return launch_gemm_pair<false, true, gk::EPI_BIAS>(p, stream);
+    if (!a_mn && !b_mn) return launch_gemm_pair<false, false, gk::EPI_BIAS>(p, stream);
+    return cudaErrorInvalidValue;
+  }
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, gk::EPI_STORE>(p, stream);
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, gk::EPI_STORE>(p, stream);
+  if (a_mn && b_mn) return launch_gemm_pair<true, true, gk::EPI_STORE>(p, stream);
+  return launch_gemm_pair<true, false, gk::EPI_STORE>(p, stream);
 }
 
 cudaError_t gemm_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream) {

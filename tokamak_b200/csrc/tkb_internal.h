@@ -60,6 +60,9 @@ struct alignas(64) GemmParams {
 };
 
 cudaError_t gemm_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream);
+// The same on CTA pairs (256 x 256 tiles; tiles_m counts 256-row tiles, a
+// K-major B map has 128-row boxes).
+cudaError_t gemm_pair_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream);
 
 cudaError_t attn_fwd_tc(const FwdParams& p, int D, bool bf16, cudaStream_t stream);
 cudaError_t attn_bwd_tc(const BwdParams& p, int D, bool bf16, cudaStream_t stream);
