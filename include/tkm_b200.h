@@ -198,10 +198,15 @@ int tkb_sgd_step(const tkb_sgd_tensor *table, int n_tensors, const float *lr,
  *   c_dtype TKB_BF16 or TKB_F32 (C row-major, ldc elements per row).
  * Forward X W: (X, 0, W, 0); input gradient dY W^T: (dY, 0, W, 1); weight
  * gradient X^T dY: (X, 1, dY, 0).  lda and ldb must be multiples of 8, ldc
- * of 8 (bf16) or 4 (fp32); pointers 16-byte aligned.  bias needs a_trans 0. */
+ * of 8 (bf16) or 4 (fp32); pointers 16-byte aligned.  bias needs a_trans 0.
+ * An fp32 C whose tiles would leave the GPU's last wave mostly idle (weight
+ * gradients: few output tiles, long K) splits K into partial sums kept in
+ * `workspace` and added in a fixed order (deterministic); give it
+ * tkb_gemm_workspace(M, N, K, c_dtype) bytes, or NULL to run unsplit. */
+size_t tkb_gemm_workspace(int M, int N, int K, int c_dtype);
 int tkb_gemm(const void *A, long long lda, int a_trans, const void *B, long long ldb, int b_trans,
              void *C, long long ldc, int c_dtype, int accumulate, const float *bias,
-             int M, int N, int K, void *stream);
+             int M, int N, int K, void *workspace, size_t workspace_bytes, void *stream);
 
 /* The twin [gate | up] FC with its SwiGLU epilogue in one kernel (replaces
  * the cuBLAS GEMM of FC_TWIN_FUSED, src/tkm_gpu.cu:1207-1236, and the twin
@@ -213,6 +218,24 @@ int tkb_gemm(const void *A, long long lda, int a_trans, const void *B, long long
 int tkb_gemm_swiglu(const void *A, long long lda, const void *B, long long ldb, int F,
                     const float *bias_gate, const float *bias_up, void *GU, long long ldgu,
                     void *H, long long ldh, int M, int K, void *stream);
+
+/* The LM head and its softmax cross-entropy without the logits in memory
+ * (replaces the cuBLAS head GEMM, the Bias group and k_softmax_loss_fwd_bwd_h
+ * with kind 0, src/tkm_gpu.cu:632-682 and 1275-1284): logits = X W + bias for
+ * X [rows][d] (ldx per row), W [d][V] (ldw per row), bias [V] (may be NULL),
+ * computed tile by tile on the tcgen05 CTA-pair GEMM.  A first pass keeps
+ * per-row statistics (tile maxima, sums of exponentials, argmax, the label's
+ * logit); *loss += mean over rows of -ln(max(p_label, 1e-7)); *correct (may
+ * be NULL) += rows whose first argmax is the label; when dlogits is not
+ * NULL a second pass recomputes each tile and writes d logits = (softmax -
+ * onehot) / rows in bf16 ([rows][ldd]).  Every logit is recomputed instead of
+ * stored: the [rows][V] logits buffer is never written.  Workspace:
+ * tkb_lmhead_ce_workspace(rows, V) bytes, 256-byte aligned.  d and V must be
+ * multiples of 8. */
+size_t tkb_lmhead_ce_workspace(int rows, int V);
+int tkb_lmhead_ce(const void *X, long long ldx, const void *W, long long ldw, const float *bias,
+                  const int32_t *labels, void *dlogits, long long ldd, float *loss, int *correct,
+                  void *workspace, size_t workspace_bytes, int rows, int d, int V, void *stream);
 
 #ifdef __cplusplus
 }

@@ -48,6 +48,24 @@ def test_gemm_layouts_and_tails(a_trans, b_trans, M, N, K, out_dtype):
     assert _rel(C.float(), ref) < (TOL_BF16 if out_dtype == torch.bfloat16 else TOL_F32)
 
 
+@pytest.mark.parametrize("accumulate", [False, True])
+@pytest.mark.parametrize("M,N,K", [(512, 512, 8192), (2000, 768, 6000)])
+def test_gemm_split_k_weight_gradient(M, N, K, accumulate):
+    """Few output tiles with a long K (a weight gradient): fp32 C from K
+    split into partial sums in the workspace, added in a fixed order --
+    identical results on repeated calls."""
+    from tokamak_b200 import lib, ops
+    assert lib().tkb_gemm_workspace(M, N, K, 0) > 0  # this shape splits
+    A, B = _operands(M, N, K, True, False, seed=9)
+    C0 = torch.randn(M, N, device="cuda")
+    C1 = ops.gemm(A, B, True, False, out=C0.clone(), accumulate=accumulate)
+    C2 = ops.gemm(A, B, True, False, out=C0.clone(), accumulate=accumulate)
+    torch.cuda.synchronize()
+    assert torch.equal(C1, C2)
+    ref = _ref(A, B, True, False) + (C0 if accumulate else 0)
+    assert _rel(C1, ref) < TOL_F32
+
+
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 def test_gemm_accumulates_into_c(out_dtype):
     from tokamak_b200 import ops
@@ -131,7 +149,7 @@ def test_gemm_rejects_bad_arguments():
     x = torch.zeros(64, 64, dtype=torch.bfloat16, device="cuda")
     import ctypes
     p = ctypes.c_void_p(x.data_ptr())
-    assert L.tkb_gemm(p, 60, 0, p, 64, 0, p, 64, 1, 0, None, 64, 64, 60, None) == -1  # lda not a multiple of 8
-    assert L.tkb_gemm(p, 64, 0, p, 64, 0, p, 64, 2, 0, None, 64, 64, 64, None) == -1  # fp16 C
-    assert L.tkb_gemm(p, 64, 0, p, 64, 0, p, 64, 1, 0, None, 0, 64, 64, None) == -1   # empty M
+    assert L.tkb_gemm(p, 60, 0, p, 64, 0, p, 64, 1, 0, None, 64, 64, 60, None, 0, None) == -1  # lda % 8
+    assert L.tkb_gemm(p, 64, 0, p, 64, 0, p, 64, 2, 0, None, 64, 64, 64, None, 0, None) == -1  # fp16 C
+    assert L.tkb_gemm(p, 64, 0, p, 64, 0, p, 64, 1, 0, None, 0, 64, 64, None, 0, None) == -1   # empty M
     assert L.tkb_gemm_swiglu(p, 64, p, 64, 12, None, None, p, 64, p, 64, 64, 64, None) == -1  # F % 8

@@ -51,7 +51,10 @@ _SIGS = {
     "tkb_softmax_loss": ([_vp, _vp, _vp, _vp, _vp, _vp, _sz, _i, _i, _i, _f, _i, _vp], _i),
     "tkb_softmax_loss_noalloc": ([_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _i, _vp], _i),
     "tkb_sgd_step": ([_vp, _i, _vp, _f, _f, _vp, _vp], _i),
-    "tkb_gemm": ([_vp, _ll, _i, _vp, _ll, _i, _vp, _ll, _i, _i, _vp, _i, _i, _i, _vp], _i),
+    "tkb_gemm_workspace": ([_i, _i, _i, _i], _sz),
+    "tkb_lmhead_ce_workspace": ([_i, _i], _sz),
+    "tkb_lmhead_ce": ([_vp, _ll, _vp, _ll, _vp, _vp, _vp, _ll, _vp, _vp, _vp, _sz, _i, _i, _i, _vp], _i),
+    "tkb_gemm": ([_vp, _ll, _i, _vp, _ll, _i, _vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _sz, _vp], _i),
     "tkb_gemm_swiglu": ([_vp, _ll, _vp, _ll, _i, _vp, _vp, _vp, _ll, _vp, _ll, _i, _i, _vp], _i),
 }
 

@@ -36,9 +36,10 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int OFF_BAR = STAGES * STAGE_BYTES;
 constexpr int NBAR = 2 * STAGES + 5;   // full[S], empty[S], acc_full[2], acc_empty[2], drain
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr int SMEM = OFF_MISC + 16 + 1024;  // + slack for the 1024-byte alignment of the swizzled ring
+constexpr int OFF_BIAS = OFF_MISC + 16;       // the column tile's 256 bias values
+constexpr int SMEM = OFF_BIAS + 1024 + 1024;  // + slack for the 1024-byte alignment of the swizzled ring
 constexpr int GROUP_M = 8;
-enum { EPI_STORE = 0, EPI_BIAS = 1, EPI_SWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_BIAS = 1, EPI_SWIGLU = 2, EPI_CE_STATS = 3, EPI_CE_GRAD = 4 };
 }  // namespace gk
 
 // Tile t -> (row tile, column tile): groups of GROUP_M row tiles; inside a
@@ -60,12 +61,65 @@ TKB_DEVFN int gemm_b_col(const GemmParams& p, int tn, int i) {
   return tn * gk::BN + i * 64;
 }
 
-TKB_DEVFN float silu_f(float x) { return x / (1.0f + ex2(-1.4426950408889634f * x)); }
+TKB_DEVFN float silu_f(float x) { return __fdividef(x, 1.0f + ex2(-1.4426950408889634f * x)); }
+
+// Where a plain or bias epilogue writes: C (or a split-K partial), its row
+// stride (elements) and mode.
+struct EpiOut {
+  void* c;
+  long long ldc;
+  int accumulate, out_f32;
+};
+
+// The 128 epilogue threads (warps 2-5) bring the column tile's bias values
+// into shared memory once per tile: sb[0..255] for the bias epilogue; the
+// gate bias in sb[0..127] and the up bias in sb[128..255] for SwiGLU.
+// Named barrier 1 (the epilogue warps only); the caller syncs before reuse.
+template <int EPI>
+TKB_DEVFN void epi_stage_bias(const GemmParams& p, float* sb, int tn) {
+  const int e = static_cast<int>(threadIdx.x) - 64;
+  if constexpr (EPI == gk::EPI_SWIGLU) {
+    const int n = tn * 128 + e;
+    sb[e] = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+    sb[128 + e] = (p.bias2 && n < p.N) ? p.bias2[n] : 0.f;
+  } else {
+#pragma unroll
+    for (int j = e; j < 256; j += 128) {
+      const int n = tn * 256 + j;
+      sb[j] = (p.bias && n < p.N) ? p.bias[n] : 0.f;
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Before an epilogue tile: the epilogue warps agree on going on (one of them
+// may have given up a wait) and, for the bias epilogues, stage the bias.
+// Returns false when the CTA aborts.
+template <int EPI>
+TKB_DEVFN bool epi_begin(const GemmParams& p, float* sb, int tn, volatile int* abort_flag) {
+  if constexpr (EPI == gk::EPI_STORE) {
+    return !*abort_flag;
+  } else {
+    // one decision for all 128 epilogue threads (an OR over named barrier 1),
+    // taken once every epilogue warp is past the previous tile, so that no
+    // warp waits at the next named barrier for a warp that left
+    uint32_t any;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(any)
+        : "r"(static_cast<uint32_t>(*abort_flag))
+        : "memory");
+    if (any) return false;
+    epi_stage_bias<EPI>(p, sb, tn);
+    return true;
+  }
+}
 
 // The epilogue of one accumulator tile for this thread's row: TMEM columns
 // 0..255 of the accumulator at `tacc` (this warp's lane quadrant) -> C (and H).
 template <int EPI>
-TKB_DEVFN void gemm_epilogue(const GemmParams& p, uint32_t tacc, int row, int tn) {
+TKB_DEVFN void gemm_epilogue(const GemmParams& p, const EpiOut& o, const float* sb, uint32_t tacc, int row, int tn) {
   using namespace gk;
   const bool rv = row < p.M;
   if constexpr (EPI == EPI_SWIGLU) {
@@ -86,29 +140,19 @@ TKB_DEVFN void gemm_epilogue(const GemmParams& p, uint32_t tacc, int row, int tn
       for (int v = 0; v < 4; ++v) {  // 8 columns per 16-byte store
         const int c8 = col + v * 8;
         if (c8 >= F) break;
-        float gv[8], uv[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          gv[j] = __uint_as_float(g[v * 8 + j]);
-          uv[j] = __uint_as_float(u[v * 8 + j]);
-        }
         uint32_t pg[4], pu[4], ph[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          pg[j] = pack2<true>(gv[2 * j], gv[2 * j + 1]);
-          pu[j] = pack2<true>(uv[2 * j], uv[2 * j + 1]);
+          pg[j] = pack2<true>(__uint_as_float(g[v * 8 + 2 * j]), __uint_as_float(g[v * 8 + 2 * j + 1]));
+          pu[j] = pack2<true>(__uint_as_float(u[v * 8 + 2 * j]), __uint_as_float(u[v * 8 + 2 * j + 1]));
         }
-        // the twin epilogue reads the stored (bf16) gate and up values, as the unfused path does
-        float hv[8];
+        // from the stored (bf16) gate and up values, as the unfused twin epilogue reads them
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float2 g2 = unpack2<true>(pg[j]), u2 = unpack2<true>(pu[j]);
-          const int n = c8 + 2 * j;
-          const float bg0 = p.bias ? p.bias[min(n, F - 1)] : 0.f, bg1 = p.bias ? p.bias[min(n + 1, F - 1)] : 0.f;
-          const float bu0 = p.bias2 ? p.bias2[min(n, F - 1)] : 0.f, bu1 = p.bias2 ? p.bias2[min(n + 1, F - 1)] : 0.f;
-          hv[2 * j] = silu_f(g2.x + bg0) * (u2.x + bu0);
-          hv[2 * j + 1] = silu_f(g2.y + bg1) * (u2.y + bu1);
-          ph[j] = pack2<true>(hv[2 * j], hv[2 * j + 1]);
+          const int nl = c + v * 8 + 2 * j;  // column within the tile
+          ph[j] = pack2<true>(silu_f(g2.x + sb[nl]) * (u2.x + sb[128 + nl]),
+                              silu_f(g2.y + sb[nl + 1]) * (u2.y + sb[128 + nl + 1]));
         }
         if (c8 + 8 <= F) {
           *reinterpret_cast<uint4*>(gu_row + c8) = make_uint4(pg[0], pg[1], pg[2], pg[3]);
@@ -126,6 +170,85 @@ TKB_DEVFN void gemm_epilogue(const GemmParams& p, uint32_t tacc, int row, int tn
         }
       }
     }
+  } else if constexpr (EPI == EPI_CE_STATS) {
+    // one pass over the row's 256 logits (+ bias): running max with the first
+    // index reaching it, sum of exp(x - max) rescaled when the max grows, and
+    // the label's logit when the label falls in this tile
+    constexpr float kLog2e = 1.4426950408889634f;
+    const int n0 = tn * BN;
+    const int lab = rv ? p.labels[row] : -1;
+    float m = -INFINITY, ssum = 0.f, labv = 0.f;
+    int am = -1;
+    bool has_lab = false;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tacc + c, r);
+      wait_ld_dep(r);
+      float v[32], cm = -INFINITY;
+      int ci = -1;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = n0 + c + j;
+        v[j] = col < p.N ? __uint_as_float(r[j]) + sb[c + j] : -INFINITY;
+        if (v[j] > cm) {
+          cm = v[j];
+          ci = col;
+        }
+        if (col == lab) {
+          labv = v[j];
+          has_lab = true;
+        }
+      }
+      if (cm > m) {
+        ssum *= ex2((m - cm) * kLog2e);
+        m = cm;
+        am = ci;
+      }
+      const float mb = m * kLog2e;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ssum += ex2(fmaf(v[j], kLog2e, -mb));
+    }
+    if (rv) {
+      p.ce_part[static_cast<long long>(row) * p.tiles_n + tn] = make_float4(m, ssum, __int_as_float(am), 0.f);
+      if (has_lab) p.ce_lab[row] = labv;
+    }
+  } else if constexpr (EPI == EPI_CE_GRAD) {
+    // d logits = (softmax - onehot) / rows, from the recomputed tile and the row's LSE
+    constexpr float kLog2e = 1.4426950408889634f;
+    const int n0 = tn * BN;
+    const int lab = rv ? p.labels[row] : -1;
+    const float lse2 = rv ? p.ce_lse[row] * kLog2e : 0.f;
+    uint16_t* drow = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tacc + c, r);
+      wait_ld_dep(r);
+      const int col = n0 + c;
+      if (!rv || col >= p.N) continue;
+      uint32_t w[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float g2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = col + 2 * j + e;
+          const float x = __uint_as_float(r[2 * j + e]) + sb[c + 2 * j + e];
+          g2[e] = (ex2(fmaf(x, kLog2e, -lse2)) - (cc == lab ? 1.f : 0.f)) * p.ce_scale;
+        }
+        w[j] = pack2<true>(g2[0], g2[1]);
+      }
+      if (col + 32 <= p.N) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          reinterpret_cast<uint4*>(drow + col)[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col + j < p.N) drow[col + j] = static_cast<uint16_t>(w[j >> 1] >> ((j & 1) * 16));
+      }
+    }
   } else {
     const int n0 = tn * BN;
 #pragma unroll 1
@@ -139,41 +262,39 @@ TKB_DEVFN void gemm_epilogue(const GemmParams& p, uint32_t tacc, int row, int tn
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
       if constexpr (EPI == EPI_BIAS) {
-        if (p.bias) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] += p.bias[min(col + j, p.N - 1)];
-        }
+        for (int j = 0; j < 32; ++j) v[j] += sb[c + j];
       }
       const bool whole = col + 32 <= p.N;
-      if (p.out_f32) {
-        float* dst = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+      if (o.out_f32) {
+        float* dst = static_cast<float*>(o.c) + static_cast<long long>(row) * o.ldc + col;
         if (whole) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-            if (p.accumulate) {
+            float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            if (o.accumulate) {
               const float4 old = reinterpret_cast<const float4*>(dst)[j];
-              o.x += old.x;
-              o.y += old.y;
-              o.z += old.z;
-              o.w += old.w;
+              w.x += old.x;
+              w.y += old.y;
+              w.z += old.z;
+              w.w += old.w;
             }
-            reinterpret_cast<float4*>(dst)[j] = o;
+            reinterpret_cast<float4*>(dst)[j] = w;
           }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (col + j < p.N) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
+            if (col + j < p.N) dst[j] = o.accumulate ? dst[j] + v[j] : v[j];
         }
       } else {
-        uint16_t* dst = static_cast<uint16_t*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+        uint16_t* dst = static_cast<uint16_t*>(o.c) + static_cast<long long>(row) * o.ldc + col;
         if (whole) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float w[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) w[e] = v[8 * j + e];
-            if (p.accumulate) {
+            if (o.accumulate) {
               const uint4 old = reinterpret_cast<const uint4*>(dst)[j];
               const uint32_t ow[4] = {old.x, old.y, old.z, old.w};
 #pragma unroll
@@ -191,7 +312,7 @@ TKB_DEVFN void gemm_epilogue(const GemmParams& p, uint32_t tacc, int row, int tn
           for (int j = 0; j < 32; ++j) {
             if (col + j >= p.N) continue;
             float w = v[j];
-            if (p.accumulate) w += __uint_as_float(static_cast<uint32_t>(dst[j]) << 16);
+            if (o.accumulate) w += __uint_as_float(static_cast<uint32_t>(dst[j]) << 16);
             dst[j] = static_cast<uint16_t>(pack2<true>(w, 0.f) & 0xFFFFu);
           }
         }
@@ -320,16 +441,19 @@ __global__ void __launch_bounds__(gk::THREADS, 1) gemm_tc_kernel(const __grid_co
     // ------------------------------------------------------------ epilogue (warps 2-5)
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    float* sb = reinterpret_cast<float*>(smem + OFF_BIAS);
+    const EpiOut out{p.c, p.ldc, p.accumulate, p.out_f32};
     int tc = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
       int tm, tn;
       gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
       const int ab = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
-      if (!mbar_wait(&acc_full[ab], aph, abort_flag)) break;
+      mbar_wait(&acc_full[ab], aph, abort_flag);
+      if (!epi_begin<EPI>(p, sb, tn, abort_flag)) break;
       tc_fence_after();
       const int row = tm * BM + q * 32 + lane;
-      gemm_epilogue<EPI>(p, tmem + lane_off + ab * BN, row, tn);
+      gemm_epilogue<EPI>(p, out, sb, tmem + lane_off + ab * BN, row, tn);
       tc_fence_before();
       mbar_arrive(&acc_empty[ab]);
     }
@@ -365,7 +489,8 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int OFF_BAR = STAGES * STAGE_BYTES;
 constexpr int NBAR = 2 * STAGES + 5;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr int SMEM = OFF_MISC + 16 + 1024;
+constexpr int OFF_BIAS = OFF_MISC + 16;
+constexpr int SMEM = OFF_BIAS + 1024 + 1024;
 }  // namespace gk2
 
 template <int EPI>
@@ -392,7 +517,8 @@ __global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int cluster = static_cast<int>(blockIdx.x >> 1), nclusters = static_cast<int>(gridDim.x >> 1);
-  const int ntiles = p.tiles_m * p.tiles_n;
+  const int ntiles_mn = p.tiles_m * p.tiles_n;
+  const int ntiles = ntiles_mn * p.splits;  // (tile, K split) work items
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -427,10 +553,11 @@ __global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid
       bool ok = true;
       for (int t = cluster; ok && t < ntiles; t += nclusters) {
         int tm, tn;
-        gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
+        gemm_tile(t % ntiles_mn, p.tiles_m, p.tiles_n, tm, tn);
+        const int kb0 = (t / ntiles_mn) * p.kb_per_split, kb1 = min(nk, kb0 + p.kb_per_split);
         const int m0 = tm * 256 + static_cast<int>(rank) * BM;
         const int nb = gemm_pair_b_col<EPI>(p, tn, rank);
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!(ok = mbar_wait(&empty[s], ph ^ 1, abort_flag))) break;
@@ -480,7 +607,8 @@ __global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid
         if (!(ok = mbar_wait_cluster(&acc_empty[ab], aph ^ 1, abort_flag))) break;
         tc_fence_after();
         const uint32_t d = tmem + ab * BN;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        const int kb0 = (t / ntiles_mn) * p.kb_per_split, kb1 = min(nk, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!(ok = mbar_wait_cluster(&full[s], ph, abort_flag))) break;
@@ -490,7 +618,7 @@ __global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t ad = A_MN ? sdesc_sw128(a + kk * 2048, 8192, 1024) : sdesc_sw128(a + kk * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b + kk * 2048, 8192, 1024) : sdesc_sw128(b + kk * 32, 16, 1024);
-            umma_pair_ss(d, ad, bd, idesc, (kb | kk) ? 1u : 0u);
+            umma_pair_ss(d, ad, bd, idesc, (kb != kb0 || kk) ? 1u : 0u);
           }
           umma_pair_commit(&empty[s], 0x3);  // both CTAs' stage s is free once these MMAs read it
         }
@@ -507,16 +635,23 @@ __global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid
     const int q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    float* sb = reinterpret_cast<float*>(smem + OFF_BIAS);
     int tc = 0;
     for (int t = cluster; t < ntiles; t += nclusters, ++tc) {
       int tm, tn;
-      gemm_tile(t, p.tiles_m, p.tiles_n, tm, tn);
+      gemm_tile(t % ntiles_mn, p.tiles_m, p.tiles_n, tm, tn);
+      const int split = t / ntiles_mn;
       const int ab = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
-      if (!mbar_wait(&acc_full[ab], aph, abort_flag)) break;
+      mbar_wait(&acc_full[ab], aph, abort_flag);
+      if (!epi_begin<EPI>(p, sb, tn, abort_flag)) break;
       tc_fence_after();
       const int row = tm * 256 + static_cast<int>(rank) * BM + q * 32 + lane;
-      gemm_epilogue<EPI>(p, tmem + lane_off + ab * BN, row, tn);
+      // split-K partials go to the workspace, [split][M][N], overwritten
+      const EpiOut out = p.splits > 1
+                             ? EpiOut{p.ws + static_cast<long long>(split) * p.M * p.N, p.N, 0, 1}
+                             : EpiOut{p.c, p.ldc, p.accumulate, p.out_f32};
+      gemm_epilogue<EPI>(p, out, sb, tmem + lane_off + ab * BN, row, tn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc_empty_leader + static_cast<uint32_t>(ab) * 8u);
@@ -532,6 +667,109 @@ __global__ void __launch_bounds__(gk2::THREADS, 1) gemm_pair_kernel(const __grid
   }
 }
 
+// C[M][N] (+)= sum over s = 0..splits-1 of ws[s][M][N], in that order (fp32).
+__global__ void __launch_bounds__(256) gemm_splitk_reduce_kernel(const float* __restrict__ ws, int splits, int M,
+                                                                 int N, float* __restrict__ c, long long ldc,
+                                                                 int accumulate) {
+  const long long MN = static_cast<long long>(M) * N;
+  if ((N & 3) == 0 && (ldc & 3) == 0) {
+    for (long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < MN;
+         i += static_cast<long long>(gridDim.x) * blockDim.x * 4) {
+      float4 acc = reinterpret_cast<const float4*>(ws + i)[0];
+      for (int s = 1; s < splits; ++s) {
+        const float4 v = reinterpret_cast<const float4*>(ws + s * MN + i)[0];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const long long r = i / N, col = i % N;
+      float4* dst = reinterpret_cast<float4*>(c + r * ldc + col);
+      if (accumulate) {
+        const float4 o = *dst;
+        acc.x += o.x;
+        acc.y += o.y;
+        acc.z += o.z;
+        acc.w += o.w;
+      }
+      *dst = acc;
+    }
+  } else {
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < MN;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+      float acc = ws[i];
+      for (int s = 1; s < splits; ++s) acc += ws[s * MN + i];
+      float* dst = c + (i / N) * ldc + i % N;
+      *dst = accumulate ? *dst + acc : acc;
+    }
+  }
+}
+
+// One warp per row: LSE = M + ln(sum_t s_t exp(m_t - M)) over the row's tile
+// partials (M = max_t m_t); the argmax is the first index of the first tile
+// reaching M (each tile kept its first maximum).
+__global__ void __launch_bounds__(256) ce_combine_kernel(const float4* __restrict__ part, int tiles_n,
+                                                         const float* __restrict__ lab_logit,
+                                                         const int* __restrict__ labels, float* __restrict__ lse,
+                                                         float* __restrict__ row_loss, int* __restrict__ correct,
+                                                         int rows, float inv_rows) {
+  const int row = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* pr = part + static_cast<long long>(row) * tiles_n;
+  float m = -INFINITY;
+  int first = 0x7FFFFFFF;
+  for (int t = lane; t < tiles_n; t += 32) {
+    const float mt = pr[t].x;
+    if (mt > m) {
+      m = mt;
+      first = t;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const int f2 = __shfl_xor_sync(0xffffffffu, first, o);
+    if (m2 > m || (m2 == m && f2 < first)) {
+      m = m2;
+      first = f2;
+    }
+  }
+  float s = 0.f;
+  for (int t = lane; t < tiles_n; t += 32) {
+    const float4 v = pr[t];
+    s += v.y * ex2((v.x - m) * 1.4426950408889634f);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    const float l = m + lg2(s) * 0.6931471805599453f;
+    lse[row] = l;
+    // -ln(max(p_label, 1e-7)) = min(LSE - label logit, -ln(1e-7))
+    row_loss[row] = fminf(l - lab_logit[row], 16.11809565095832f) * inv_rows;
+    const int am = __float_as_int(pr[first].z);
+    if (correct && am == labels[row]) atomicAdd(correct, 1);
+  }
+}
+
+cudaError_t ce_combine(const float4* part, int tiles_n, const float* lab_logit, const int* labels, float* lse,
+                       float* row_loss, int* correct, int rows, float inv_rows, cudaStream_t stream) {
+  const unsigned grid = static_cast<unsigned>((static_cast<long long>(rows) * 32 + 255) / 256);
+  ce_combine_kernel<<<grid, 256, 0, stream>>>(part, tiles_n, lab_logit, labels, lse, row_loss, correct, rows,
+                                              inv_rows);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_splitk_reduce(const GemmParams& p, cudaStream_t stream) {
+  const long long MN = static_cast<long long>(p.M) * p.N;
+  long long blocks = (MN / 4 + 255) / 256 + 1;
+  if (blocks > 148LL * 8) blocks = 148LL * 8;
+  const unsigned grid = static_cast<unsigned>(blocks);
+  gemm_splitk_reduce_kernel<<<grid, 256, 0, stream>>>(p.ws, p.splits, p.M, p.N, static_cast<float*>(p.c), p.ldc,
+                                                      p.accumulate);
+  return cudaGetLastError();
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 static cudaError_t launch_gemm_pair(const GemmParams& p, cudaStream_t stream) {
   auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
@@ -539,7 +777,7 @@ static cudaError_t launch_gemm_pair(const GemmParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int ntiles = p.tiles_m * p.tiles_n;
+  const int ntiles = p.tiles_m * p.tiles_n * p.splits;
   const int nclusters = min(ntiles, sms / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * nclusters));
@@ -570,6 +808,11 @@ static cudaError_t launch_gemm(const GemmParams& p, cudaStream_t stream) {
 }
 
 cudaError_t gemm_pair_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream) {
+  if (epi == gk::EPI_CE_STATS || epi == gk::EPI_CE_GRAD) {
+    if (a_mn || !b_mn) return cudaErrorInvalidValue;
+    return epi == gk::EPI_CE_STATS ? launch_gemm_pair<false, true, gk::EPI_CE_STATS>(p, stream)
+                                   : launch_gemm_pair<false, true, gk::EPI_CE_GRAD>(p, stream);
+  }
   if (epi == gk::EPI_SWIGLU) {
     if (a_mn || !b_mn) return cudaErrorInvalidValue;
     return launch_gemm_pair<false, true, gk::EPI_SWIGLU>(p, stream);

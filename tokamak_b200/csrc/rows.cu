@@ -1305,6 +1305,12 @@ static cudaError_t softmax_bwd_t(const void* p, const void* dp, void* dx, int ro
   return cudaGetLastError();
 }
 
+// loss += sum(row_loss) in the fixed order of sum_rows_kernel (used by the fused LM-head loss)
+cudaError_t sum_rows(const float* row_loss, int rows, float* loss, cudaStream_t st) {
+  sum_rows_kernel<<<1, 256, 0, st>>>(row_loss, rows, loss);
+  return cudaGetLastError();
+}
+
 template <typename T>
 static cudaError_t softmax_loss_t(const void* logits, const int32_t* labels, void* dlogits, float* loss, int* correct,
                                   float* row_loss, int rows, int C, int kind, float gamma, cudaStream_t st) {

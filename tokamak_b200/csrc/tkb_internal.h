@@ -57,12 +57,27 @@ struct alignas(64) GemmParams {
   int b_split;                // SwiGLU: column of B where the up half starts (F)
   int accumulate;             // C += result
   int out_f32;                // C is fp32 (else bf16)
+  int splits;                 // CTA-pair form, fp32 C: K split over this many partial sums (1: none)
+  int kb_per_split;           // 64-deep K blocks per split
+  float* ws;                  // splits > 1: partial sums [splits][M][N], summed into C in split order
+  // LM head + softmax cross-entropy (C = logits + bias, never stored):
+  const int* labels;          // [M] class of each row
+  float4* ce_part;            // statistics pass: [M][tiles_n] (tile max, sum of exp(x - max), argmax bits, 0)
+  float* ce_lab;              // statistics pass: [M] the label's logit
+  const float* ce_lse;        // gradient pass: [M] log-sum-exp of each row
+  float ce_scale;             // gradient pass: 1 / rows
 };
 
 cudaError_t gemm_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream);
 // The same on CTA pairs (256 x 256 tiles; tiles_m counts 256-row tiles, a
 // K-major B map has 128-row boxes).
 cudaError_t gemm_pair_tc(const GemmParams& p, bool a_mn, bool b_mn, int epi, cudaStream_t stream);
+// C (+)= sum over s of ws[s][M][N], s in order (the split-K partials; fp32 C).
+cudaError_t gemm_splitk_reduce(const GemmParams& p, cudaStream_t stream);
+// Per row: LSE from the statistics pass's tile partials, the cross-entropy
+// term min(LSE - label logit, -ln 1e-7) / rows into row_loss, correct += argmax == label.
+cudaError_t ce_combine(const float4* part, int tiles_n, const float* lab_logit, const int* labels, float* lse,
+                       float* row_loss, int* correct, int rows, float inv_rows, cudaStream_t stream);
 
 cudaError_t attn_fwd_tc(const FwdParams& p, int D, bool bf16, cudaStream_t stream);
 cudaError_t attn_bwd_tc(const BwdParams& p, int D, bool bf16, cudaStream_t stream);

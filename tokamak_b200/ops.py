@@ -183,8 +183,9 @@ def gemm(A, B, a_trans=False, b_trans=False, out=None, out_dtype=None, accumulat
     N = B.shape[0] if b_trans else B.shape[1]
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype or torch.bfloat16, device=A.device)
+    ws, nws = _ws(lib().tkb_gemm_workspace(M, N, K, dtype_code(out)), A.device)
     check(lib().tkb_gemm(_p(A), A.stride(0), int(a_trans), _p(B), B.stride(0), int(b_trans), _p(out), out.stride(0),
-                         dtype_code(out), int(accumulate), _p(bias), M, N, K, _stream()), "tkb_gemm")
+                         dtype_code(out), int(accumulate), _p(bias), M, N, K, _p(ws), nws, _stream()), "tkb_gemm")
     return out
 
 
@@ -196,3 +197,18 @@ def gemm_swiglu(A, B, F, bias_gate=None, bias_up=None):
     check(lib().tkb_gemm_swiglu(_p(A), A.stride(0), _p(B), B.stride(0), F, _p(bias_gate), _p(bias_up), _p(gu),
                                 gu.stride(0), _p(h), h.stride(0), M, K, _stream()), "tkb_gemm_swiglu")
     return gu, h
+
+
+def lmhead_ce(X, W, labels, bias=None, want_grad=True):
+    """(loss, d logits or None, correct) of softmax cross-entropy over
+    logits = X W + bias, without storing the logits (tkb_lmhead_ce)."""
+    rows, d = X.shape
+    V = W.shape[1]
+    loss = torch.zeros(1, dtype=torch.float32, device=X.device)
+    corr = torch.zeros(1, dtype=torch.int32, device=X.device)
+    dl = torch.empty(rows, V, dtype=torch.bfloat16, device=X.device) if want_grad else None
+    ws, nws = _ws(lib().tkb_lmhead_ce_workspace(rows, V), X.device)
+    check(lib().tkb_lmhead_ce(_p(X), X.stride(0), _p(W), W.stride(0), _p(bias), _p(labels), _p(dl),
+                              dl.stride(0) if dl is not None else 0, _p(loss), _p(corr), _p(ws), nws, rows, d, V,
+                              _stream()), "tkb_lmhead_ce")
+    return loss, dl, corr
