@@ -922,12 +922,33 @@ def run_gemm(args):
     rows.append({"name": "gate|up fwd + SwiGLU epilogue", "M": 16384, "N": 2 * F, "K": 2048, "ms": ours,
                  "tflops": fl / (ours * 1e-3) / 1e12, "cublas_ms": ref, "cublas_tflops": fl / (ref * 1e-3) / 1e12,
                  "cublas_path": "torch.matmul + torch SiLU*up"})
+    # the LM head with its softmax CE (configuration 4: 16384 rows, d 2048, vocab 32000): fused
+    # (tkb_lmhead_ce: statistics pass + gradient pass, no logits buffer) against cuBLAS GEMM
+    # + bias + tkb_softmax_loss (the unfused path's kernels)
+    Rh, dh, Vh = 16384, 2048, 32000
+    X = (0.5 * torch.randn(Rh, dh, device=dev, generator=g)).bfloat16()
+    Wh = (0.02 * torch.randn(dh, Vh, device=dev, generator=g)).bfloat16()
+    bh = torch.zeros(Vh, device=dev)
+    yh = torch.randint(0, Vh, (Rh,), device=dev, generator=g, dtype=torch.int32)
+    fused = timed(lambda: ops.lmhead_ce(X, Wh, yh, bh))
+
+    def unfused():
+        logits = torch.matmul(X, Wh) + bh.bfloat16()
+        return ops.softmax_loss(logits, yh, 0, 2.0)
+    ref_ce = timed(unfused)
+    fl = 2.0 * Rh * dh * Vh
+    ce_row = {"name": "lm-head + softmax CE (fused, two GEMM passes, no logits buffer)", "M": Rh, "N": Vh, "K": dh,
+              "ms": fused, "unfused_ms": ref_ce,
+              "unfused_path": "cuBLAS GEMM + bias + tkb_softmax_loss (logits [16384 x 32000] bf16 written and read)",
+              "logits_buffer_bytes_saved": Rh * Vh * 2}
+    del X, Wh, bh, yh
     launches = int(L.tkb_launch_count() - n0)
     tot_fl = sum(2.0 * r["M"] * r["N"] * r["K"] for r in rows[:-1])
     tot_ms = sum(r["ms"] for r in rows[:-1])
     tot_cb = sum(r["cublas_ms"] for r in rows[:-1])
     value = tot_fl / (tot_ms * 1e-3) / 1e12
     dom = max(rows[:-1], key=lambda r: r["ms"])
+    rows.append(ce_row)
     if rank == 0:
         print(json.dumps({
             "metric": "bf16 GEMM TFLOP/s (configuration-4 layer GEMMs + LM head)", "value": value,
@@ -935,6 +956,7 @@ def run_gemm(args):
             "ms_per_step": tot_ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0, 0.05)", "config": {"workload": "gemm_c4", "l2": "256 MB flush before every launch"},
             "cublas_tflops_same_shapes": tot_fl / (tot_cb * 1e-3) / 1e12, "kernels": rows,
+            "gemm_tflops_vs_cublas": value / (tot_fl / (tot_cb * 1e-3) / 1e12),
             "roofline": {"bound": "tensor", "kernel": dom["name"], "achieved": dom["tflops"], "peak": peak,
                          "unit": "TFLOP/s", "frac": dom["tflops"] / peak,
                          "peak_source": f"{src} bf16 burst (MEASURED_PEAKS.json)", "traffic": None},

@@ -42,7 +42,8 @@ def random_params(orc, rng, scale=0.02, gain_sd=0.1, bias_sd=0.02):
     return [np.asarray(a, np.float32) for a in out]
 
 
-def compare_step(dsl, batch, dtype, rng, tol_loss, tol_logits, tol_grad, labels_fn=None, lr=0.0, x=None):
+def compare_step(dsl, batch, dtype, rng, tol_loss, tol_logits, tol_grad, labels_fn=None, lr=0.0, x=None,
+                 check_logits=True):
     rt_mod = runtime_mod()
     orc = oracle_for(dsl, batch)
     params = random_params(orc, rng)
@@ -61,8 +62,9 @@ def compare_step(dsl, batch, dtype, rng, tol_loss, tol_logits, tol_grad, labels_
     ref = orc.run(x.astype(np.float64), y)
     loss = rt.step(x, y, lr)
     assert abs(loss - ref["loss"]) <= tol_loss * abs(ref["loss"]), (loss, ref["loss"])
-    logits = rt.logits(rows * C)
-    assert rel_l2(logits, ref["acts"][orc.nodes[loss_node].in0].ravel()) <= tol_logits
+    if check_logits:
+        logits = rt.logits(rows * C)
+        assert rel_l2(logits, ref["acts"][orc.nodes[loss_node].in0].ravel()) <= tol_logits
     assert rel_l2(rt.input_grad(), ref["dinput"].ravel()) <= tol_grad
     worst = 0.0
     for t, (node, kind, size) in enumerate(orc.tensors):
@@ -367,15 +369,35 @@ def test_residual_whose_skip_is_the_group_input(dtype_name):
     rt.close()
 
 
+@pytest.mark.parametrize("swiglu", [False, True], ids=["gemm", "gemm+swiglu"])
 @pytest.mark.parametrize("batch", [4, 64], ids=["c1", "8192_rows"])
-def test_engine_step_on_the_tcgen05_gemm(monkeypatch, batch):
+def test_engine_step_on_the_tcgen05_gemm(monkeypatch, batch, swiglu):
     """The configuration-1 model (one layer at 8192 rows, or both layers at
     512) with its FC GEMMs -- forward, input gradient and weight gradient --
-    on libtkm_b200's tcgen05 kernel (TKM_GEMM=tc) instead of cuBLAS."""
+    on libtkm_b200's tcgen05 kernel (TKM_GEMM=tc) instead of cuBLAS, and with
+    each SwiGLU group computed in its twin GEMM's epilogue (TKM_GEMM_SWIGLU=1)."""
     from tokamak_b200.configs import C1, dsl_for
     monkeypatch.setenv("TKM_GEMM", "tc")
+    if swiglu:
+        monkeypatch.setenv("TKM_GEMM_SWIGLU", "1")
+    else:
+        monkeypatch.delenv("TKM_GEMM_SWIGLU", raising=False)
     rt_mod = runtime_mod()
     cfg = dict(C1, layers=1, batch=batch) if batch > 4 else C1
     rt, *_ = compare_step(dsl_for(cfg), cfg["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(40 + batch),
                           1e-2, 2e-2, 5e-2)
+    rt.close()
+
+
+def test_engine_step_with_fused_lm_head_cross_entropy(monkeypatch):
+    """TKM_FUSED_CE=1: the head FC, its Bias group and the softmax CE of the
+    configuration-1 model run as one tkb_lmhead_ce call (no logits buffer is
+    written); loss, d(input) and every parameter gradient -- the head's weight
+    and bias included -- match the oracle."""
+    from tokamak_b200.configs import C1, dsl_for
+    monkeypatch.setenv("TKM_GEMM", "tc")
+    monkeypatch.setenv("TKM_FUSED_CE", "1")
+    rt_mod = runtime_mod()
+    rt, *_ = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(77), 1e-2, 2e-2, 5e-2,
+                          check_logits=False)
     rt.close()
