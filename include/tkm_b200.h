@@ -43,6 +43,11 @@ const char *tkb_last_error(void);
 int tkb_device_error(unsigned int *code, void *stream);
 /* Number of kernels this library launched since load (all entry points). */
 unsigned long long tkb_launch_count(void);
+/* Self-test of the failure path (no counterpart in the reference): one
+ * kernel waits, for at most limit_ns (<= 2 s), on an mbarrier that nothing
+ * arrives on, gives up like a pipeline kernel whose partner stopped, and
+ * records bit 0 in the device error word (read it with tkb_device_error). */
+int tkb_selftest_wait_timeout(unsigned long long limit_ns, void *stream);
 
 /* ------------------------------------------------------------ attention
  * Packed layout of the reference (src/tkm_gpu.cu:331-338, 366-368):

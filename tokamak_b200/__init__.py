@@ -30,6 +30,7 @@ _SIGS = {
     "tkb_version": ([], ctypes.c_char_p),
     "tkb_last_error": ([], ctypes.c_char_p),
     "tkb_device_error": ([ctypes.POINTER(ctypes.c_uint), _vp], _i),
+    "tkb_selftest_wait_timeout": ([ctypes.c_ulonglong, _vp], _i),
     "tkb_launch_count": ([], ctypes.c_ulonglong),
     "tkb_gqa_attn_fwd": ([_vp, _vp, _vp, _i, _i, _i, _i, _i, _f, _i, _i, _vp], _i),
     "tkb_gqa_attn_bwd_workspace": ([_i, _i, _i, _i, _i], _sz),

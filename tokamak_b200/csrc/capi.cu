@@ -69,6 +69,36 @@ int tkb_device_error(unsigned int* code, void* stream) {
   return TKB_OK;
 }
 
+// ------------------------------------------------------------------ self-test
+}  // extern "C"
+
+namespace tkb {
+// Waits, with a limit of limit_ns, on an mbarrier that nothing arrives on:
+// the bounded-wait path every pipeline kernel takes when a partner role
+// stops, run on purpose.  The wait ends by itself and records the code.
+__global__ void wait_timeout_selftest_kernel(unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_limit(&bar, 0, &abort_flag, limit_ns);
+  __syncthreads();
+}
+}  // namespace tkb
+
+extern "C" {
+
+int tkb_selftest_wait_timeout(unsigned long long limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > 2000000000ull)
+    return fail(TKB_ERR_ARG, "tkb_selftest_wait_timeout: limit must be in (0, 2 s]");
+  tkb::wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns);
+  return cuda_status(cudaGetLastError(), "tkb_selftest_wait_timeout", 1);
+}
+
 // ------------------------------------------------------------------ attention
 int tkb_gqa_attn_fwd(const void* qkv, void* out, float* lse, int B, int S, int Hq, int Hkv, int D, float scale,
                      int causal, int dtype, void* stream) {

@@ -89,6 +89,22 @@ TKB_DEVFN bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fla
   }
 }
 
+// The same with a caller-chosen limit (the self-test of the timeout path).
+TKB_DEVFN bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                               unsigned long long limit_ns) {
+  const uint32_t a = smem_u32(bar);
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(a, parity)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > limit_ns) {
+      atomicOr(&g_device_error, ERR_WAIT_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- TMA
 TKB_DEVFN void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -102,6 +118,15 @@ TKB_DEVFN void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int x
       " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(cache_policy)
       : "memory");
+}
+
+// Request a 3-D tile into L2 only (no shared memory, no completion to wait
+// for): brings a later load's data closer while the ring is full.
+TKB_DEVFN void tma_prefetch_3d(const CUtensorMap* m, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
 }
 
 // 2-D tiled load (x innermost).  x * element size must be a multiple of 16 B.
@@ -120,6 +145,13 @@ TKB_DEVFN void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Start bringing `bytes` (a multiple of 16, 16-byte aligned) into L2 without
+// waiting for them: more bytes in flight from DRAM than the shared-memory ring holds.
+TKB_DEVFN void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
 }
 
 // The same with an L2 cache policy (createpolicy).
