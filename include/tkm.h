@@ -279,7 +279,8 @@ TKM_API int tkm_load_optimizer_buffer(TkmRuntime *rt, const void *buffer, size_t
  * the caller sends it to every rank (any transport), then each rank calls
  * tkm_runtime_init_dp before its first step.  Every step then averages the
  * gradients of all ranks with one all-reduce inside the captured step graph
- * before the SGD update.  Returns 1 on success. */
+ * before the SGD update (a world of one rank runs the same exchange, an
+ * identity).  Returns 1 on success. */
 TKM_API int tkm_nccl_unique_id(void *out128);
 TKM_API int tkm_runtime_init_dp(TkmRuntime *rt, const void *unique_id128, int rank, int world_size);
 

@@ -6,7 +6,9 @@ GPU path (src/main.c:77-143, 253-304).
 
 Tolerances: fp32 mode 1e-4 relative L2 on loss, logits, input and parameter
 gradients and updated weights; bf16 mode loss within 1 %, logits within 2e-2
-and gradients within 5e-2 relative L2 (bf16 activations through every layer)."""
+and input and parameter gradients within 2e-2 relative L2 (north_star's bf16
+bound; measured worst 0.003-0.008 with bf16 activations through every layer).
+The finite-difference checks keep their own absolute bounds."""
 import numpy as np
 import pytest
 
@@ -103,7 +105,7 @@ def test_llama_c1_fp32_step_matches_oracle():
 def test_llama_c1_bf16_step_matches_oracle():
     from tokamak_b200.configs import C1, dsl_for
     rt_mod = runtime_mod()
-    rt, *_ = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(8), 1e-2, 2e-2, 5e-2)
+    rt, *_ = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(8), 1e-2, 2e-2, 2e-2)
     rt.close()
 
 
@@ -116,7 +118,7 @@ def test_llama_layer_many_rows_matches_oracle(dtype_name):
     rt_mod = runtime_mod()
     dtype = getattr(rt_mod, "DTYPE_" + dtype_name)
     cfg = dict(C1, layers=1, batch=64)
-    tols = (1e-4, 1e-4, 1e-4) if dtype_name == "F32" else (1e-2, 2e-2, 5e-2)
+    tols = (1e-4, 1e-4, 1e-4) if dtype_name == "F32" else (1e-2, 2e-2, 2e-2)
     rt, *_ = compare_step(dsl_for(cfg), cfg["batch"], dtype, np.random.default_rng(21), *tols)
     rt.close()
 
@@ -385,7 +387,7 @@ def test_engine_step_on_the_tcgen05_gemm(monkeypatch, batch, swiglu):
     rt_mod = runtime_mod()
     cfg = dict(C1, layers=1, batch=batch) if batch > 4 else C1
     rt, *_ = compare_step(dsl_for(cfg), cfg["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(40 + batch),
-                          1e-2, 2e-2, 5e-2)
+                          1e-2, 2e-2, 2e-2)
     rt.close()
 
 
@@ -398,6 +400,44 @@ def test_engine_step_with_fused_lm_head_cross_entropy(monkeypatch):
     monkeypatch.setenv("TKM_GEMM", "tc")
     monkeypatch.setenv("TKM_FUSED_CE", "1")
     rt_mod = runtime_mod()
-    rt, *_ = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(77), 1e-2, 2e-2, 5e-2,
+    rt, *_ = compare_step(dsl_for(C1), C1["batch"], rt_mod.DTYPE_BF16, np.random.default_rng(77), 1e-2, 2e-2, 2e-2,
                           check_logits=False)
     rt.close()
+
+
+@pytest.mark.parametrize("grad_dtype", ["F32", "BF16"])
+def test_data_parallel_exchange_on_one_rank(grad_dtype):
+    """The data-parallel exchange on a world of one rank (NCCL, inside the
+    captured step): with fp32 gradients the step is bit-identical to a
+    runtime without it; with bf16 gradients (rounded on the communication
+    stream, averaged, widened back) the weight update agrees within bf16
+    rounding.  The all-reduce timer reports the bytes sent per rank."""
+    from tokamak_b200 import runtime
+    from tokamak_b200.configs import C1, dsl_for
+    cfg = dict(C1, layers=1)
+    dsl = dsl_for(cfg)
+    rng = np.random.default_rng(3)
+    x = rng.normal(0, 1, cfg["batch"] * cfg["seq"] * cfg["d_model"]).astype(np.float32)
+    y = rng.integers(0, cfg["vocab"], cfg["batch"] * cfg["seq"]).astype(np.int32)
+    base = runtime.Runtime.from_dsl(dsl, cfg["batch"], runtime.DTYPE_BF16)
+    base.init_weights(9, 0.02)
+    w0 = base.save_weights()
+    dp = runtime.Runtime.from_dsl(dsl, cfg["batch"], runtime.DTYPE_BF16)
+    dp.load_weights(w0)
+    dp.init_dp(runtime.nccl_unique_id(), 0, 1, getattr(runtime, "DTYPE_" + grad_dtype))
+    for _ in range(3):  # eager, captured, replayed
+        base.step(x, y, 0.05)
+        dp.step(x, y, 0.05)
+    a = runtime.tkm1_unpack(base.save_weights())
+    b = runtime.tkm1_unpack(dp.save_weights())
+    start = runtime.tkm1_unpack(w0)
+    for t, (wa, wb, ws) in enumerate(zip(a, b, start)):
+        if grad_dtype == "F32":
+            assert np.array_equal(wa, wb), t
+        elif np.linalg.norm(wa - ws) > 0:
+            assert rel_l2(wb - ws, wa - ws) < 1e-2, t
+    ms, nbytes = dp.dp_allreduce_time(3)
+    assert ms > 0
+    assert nbytes % (4 if grad_dtype == "F32" else 2) == 0 and nbytes > 0
+    base.close()
+    dp.close()
