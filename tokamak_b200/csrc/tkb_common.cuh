@@ -120,15 +120,6 @@ TKB_DEVFN void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int x
       : "memory");
 }
 
-// Request a 3-D tile into L2 only (no shared memory, no completion to wait
-// for): brings a later load's data closer while the ring is full.
-TKB_DEVFN void tma_prefetch_3d(const CUtensorMap* m, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(m)),
-               "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-
 // 2-D tiled load (x innermost).  x * element size must be a multiple of 16 B.
 TKB_DEVFN void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -145,13 +136,6 @@ TKB_DEVFN void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
-}
-
-// Start bringing `bytes` (a multiple of 16, 16-byte aligned) into L2 without
-// waiting for them: more bytes in flight from DRAM than the shared-memory ring holds.
-TKB_DEVFN void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
-               : "memory");
 }
 
 // The same with an L2 cache policy (createpolicy).
