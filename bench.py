@@ -12,7 +12,9 @@ attention (default; BASELINE.json configs[1], headline shape): GQA attention
     "train"    the configs[3] data-parallel training step (below) with its
                NCCL gradient all-reduce timed alone (time, bus bandwidth);
     "longctx"  configs[4] at S=16384 with the KV-head groups sharded over
-               the N ranks.
+               the N ranks;
+    "rows"     the rows workload (below) on every rank, per-GPU GB/s and
+               each kernel's fraction of the HBM peak (skip with --no-rows).
 train: one training step of the ~1B Llama-style decoder through
   the engine API of libtkm.so (bf16, batch 8 x 2048 tokens per GPU), the step
   captured as one CUDA graph; with N > 1 ranks the gradients are averaged by
@@ -162,9 +164,11 @@ def main():
     ap.add_argument("--profile", default=None, help="write the per-launch profile (train/rows) to this JSON file")
     ap.add_argument("--no-train", action="store_true", help="default line without the train object")
     ap.add_argument("--no-longctx", action="store_true", help="default line without the longctx object")
+    ap.add_argument("--no-rows", action="store_true", help="default line without the rows object")
     ap.add_argument("--train-steps", type=int, default=10, help="timed steps of the train object")
-    ap.add_argument("--dp-grad-dtype", default="bf16", choices=["bf16", "fp32"],
-                    help="dtype the data-parallel gradients are averaged in")
+    ap.add_argument("--dp-grad-dtype", default="fp32", choices=["bf16", "fp32"],
+                    help="dtype the data-parallel gradients are averaged in (fp32: same-box step 95.6 vs 97.9 ms "
+                         "for bf16 at 2 GPUs, whose rounding and widening passes cost more than the halved bytes save)")
     ap.add_argument("--gemm-shape", default=None, help="gemm workload: run only the shape with this name")
     ap.add_argument("--gemm", default=None, choices=["cublas", "tc"],
                     help="the engine's FC GEMMs: cuBLAS (default) or the tcgen05 kernel (sets TKM_GEMM)")
@@ -198,6 +202,8 @@ def main():
                                         max(3, min(args.warmup, 5)))
     if not args.no_longctx:
         result["longctx"] = measure_longctx(args, world, rank, local, dev, args.seq or 16384, 5, 3)
+    if not args.no_rows:
+        result["rows"] = measure_rows(args, rank, 5, 3)[1]
     if rank == 0:
         print(json.dumps(result))
     dist_done(world)
@@ -687,15 +693,14 @@ def rows_cpu_baseline():
         "2048 x 4096 Add+RMSNorm fwd, 2048 x 11008 SwiGLU fwd, 1024 x 32000 softmax CE fwd+bwd"
 
 
-def run_rows(args):
+def measure_rows(args, rank, steps, warmup):
     """Generated plasma kernels at configuration 2's shapes, timed per launch
     by the engine's profiler inside a bf16 training step of the graph
     [16384 x 4096] -> FC -> Bias+Add(residual) -> RMSNorm -> twin FC(11008)
     -> Bias+SiLU * Bias -> FC, and the softmax cross-entropy over
-    [8192 x 32000] logits."""
+    [8192 x 32000] logits.  Returns (per-kernel rows, the `rows` record)."""
     from tokamak_b200 import runtime
-    world, rank, local, dev = dist_setup()
-    nrows = args.seq or 16384
+    nrows = (args.seq if args.workload == "rows" else None) or 16384
     chain = f"""input: 1x{nrows}x4096
 flow:
   r: {{
@@ -717,9 +722,9 @@ flow:
         rt = runtime.Runtime.from_dsl(dsl, 1, runtime.DTYPE_BF16)
         rt.init_weights(7, 0.02)
         x = np.random.default_rng(1).normal(0, 1, rt.input_elements).astype(np.float32)
-        for _ in range(max(3, args.warmup)):
+        for _ in range(warmup):
             rt.step(x, None, 0.0)
-        prof = rt.profile(iters=max(3, args.steps))
+        prof = rt.profile(iters=steps)
         out += [e for e in prof if e["kind"] in ("plasma", "softmax/loss")]
         rt.close()
     peak, peak_sus, hbm, src = load_peaks()
@@ -731,6 +736,23 @@ flow:
     tot_ms = sum(r["ms"] for r in rows)
     agg = tot_b / (tot_ms * 1e-3) / 1e9
     dom = max(rows, key=lambda r: r["ms"])
+    rec = {"metric": "fused row kernels achieved HBM GB/s (bf16, per GPU)", "value": agg, "unit": "GB/s",
+           "ms_per_step": tot_ms, "steps": steps, "warmup": warmup,
+           "config": {"workload": "plasma_rows", "shapes": "16384x4096 add+RMSNorm, 16384x11008 SwiGLU, 8192x32000 CE",
+                      "l2": "every tensor larger than L2"},
+           "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in r.items()} for r in rows],
+           "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": dom["GB/s"], "peak": hbm, "unit": "GB/s",
+                        "frac": dom["GB/s"] / hbm, "peak_source": f"{src} HBM copy (MEASURED_PEAKS.json)",
+                        "traffic": load_rows_traffic().get(dom["name"])}}
+    return rows, rec
+
+
+def run_rows(args):
+    """The rows workload alone (see measure_rows); with --profile the
+    per-kernel rows are also written to that file."""
+    world, rank, local, dev = dist_setup()
+    rows, rec = measure_rows(args, rank, max(3, args.steps), max(3, args.warmup))
+    agg, tot_ms, dom_rf = rec["value"], rec["ms_per_step"], rec["roofline"]
     if args.profile and rank == 0:
         with open(args.profile, "w") as f:
             json.dump(rows, f, indent=1)
@@ -743,12 +765,7 @@ flow:
             "metric": "fused row kernels achieved HBM GB/s (bf16)", "value": agg * world, "unit": "GB/s",
             "n_gpus": world, "steps": max(3, args.steps), "warmup": max(3, args.warmup), "ms_per_step": tot_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "plasma_rows", "shapes": "16384x4096 add+RMSNorm, 16384x11008 SwiGLU, 8192x32000 CE",
-                       "l2": "every tensor larger than L2"},
-            "kernels": rows,
-            "roofline": {"bound": "hbm", "kernel": dom["name"], "achieved": dom["GB/s"], "peak": hbm, "unit": "GB/s",
-                         "frac": dom["GB/s"] / hbm, "peak_source": f"{src} HBM copy (MEASURED_PEAKS.json)",
-                         "traffic": load_rows_traffic().get(dom["name"])},
+            "config": rec["config"], "kernels": rows, "roofline": dom_rf,
             "e2e": None, "cpu_baseline": cpu, "gpu_launches": len(rows)}))
     dist_done(world)
     return 0

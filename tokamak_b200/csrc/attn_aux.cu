@@ -64,7 +64,7 @@ cudaError_t make_tmap_2d(CUtensorMap* m, const void* base, long long inner, long
 // UNROLL passes with their loads issued before any reduction.
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(const void* __restrict__ out, const void* __restrict__ dout,
-                                                           const float* __restrict__ lse, float* __restrict__ lse2,
+                                                           const float* __restrict__ lse, float* __restrict__ nlse2,
                                                            float* __restrict__ delta, long long o_row_stride, long long o_batch_stride, int B,
                                                            int S, int S_pad, int Hq) {
   constexpr int LPR = D / 8, RPW = 32 / LPR, UNROLL = 4, ROWS = RPW * UNROLL;
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_kernel(const void* __restric
         const long long bh = wrow / S_pad;
         const int row = static_cast<int>(wrow % S_pad);
         delta[wrow] = row < S ? acc : 0.f;
-        lse2[wrow] = row < S ? lse[bh * S + row] * 1.4426950408889634f : INFINITY;
+        nlse2[wrow] = row < S ? lse[bh * S + row] * -1.4426950408889634f : -INFINITY;
       }
     }
   }
@@ -120,13 +120,13 @@ static int grid_for(long long work, int per_block) {
   return static_cast<int>(g < 1 ? 1 : (g > cap ? cap : g));
 }
 
-cudaError_t attn_bwd_pre(const void* out, const void* dout, const float* lse, float* lse2, float* delta,
+cudaError_t attn_bwd_pre(const void* out, const void* dout, const float* lse, float* nlse2, float* delta,
                          long long o_row_stride, long long o_batch_stride, int B, int S, int S_pad,
                          int Hq, int D, bool bf16, cudaStream_t st) {
   // 8 warps per block, each covering 8 (D = 128) or 16 (D = 64) rows per pass
   const int grid = grid_for(static_cast<long long>(B) * Hq * S_pad, 8 * (D == 64 ? 16 : 8));
 #define TKB_PRE(DD, BB) \
-  attn_bwd_pre_kernel<DD, BB><<<grid, 256, 0, st>>>(out, dout, lse, lse2, delta, o_row_stride, o_batch_stride, B, S, S_pad, Hq)
+  attn_bwd_pre_kernel<DD, BB><<<grid, 256, 0, st>>>(out, dout, lse, nlse2, delta, o_row_stride, o_batch_stride, B, S, S_pad, Hq)
   if (D == 128) { if (bf16) TKB_PRE(128, true); else TKB_PRE(128, false); }
   else if (D == 64) { if (bf16) TKB_PRE(64, true); else TKB_PRE(64, false); }
   else return cudaErrorInvalidValue;

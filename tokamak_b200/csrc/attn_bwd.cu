@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
                       i * 128, b, pol_q);
         }
         const long long ro = (static_cast<long long>(b) * p.Hq + hq) * p.S_pad + i * 128;
-        bulk_load(smem + C::OFF_LSE + s * 512, p.lse2 + ro, 512, &q_full[s]);
+        bulk_load(smem + C::OFF_LSE + s * 512, p.nlse2 + ro, 512, &q_full[s]);
         bulk_load(smem + C::OFF_DEL + s * 512, p.delta + ro, 512, &q_full[s]);
         issued = it + 1;
       }
@@ -306,15 +306,19 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
         wait_ld_dep32(v1);
         // masked keys (sequence tail) and the diagonal tile need the per-element test
         const bool need_mask = !key_ok || qmin > 0;
+        const uint64_t sl2x2 = f2(sl2, sl2);
 #pragma unroll
         for (int e4 = 0; e4 < 16; ++e4) {
-          const float4 l = lse4[e4];
+          const float4 l = lse4[e4];  // -LSE * log2(e) of queries 4 e4 .. 4 e4 + 3
           const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
           const int q0 = e4 * 4;
-          float a0 = ex2(fmaf(__uint_as_float(src[0]), sl2, -l.x));
-          float a1 = ex2(fmaf(__uint_as_float(src[1]), sl2, -l.y));
-          float a2 = ex2(fmaf(__uint_as_float(src[2]), sl2, -l.z));
-          float a3 = ex2(fmaf(__uint_as_float(src[3]), sl2, -l.w));
+          float a0, a1, a2, a3;
+          f2_split(fma_f2(f2(__uint_as_float(src[0]), __uint_as_float(src[1])), sl2x2, f2(l.x, l.y)), a0, a1);
+          f2_split(fma_f2(f2(__uint_as_float(src[2]), __uint_as_float(src[3])), sl2x2, f2(l.z, l.w)), a2, a3);
+          a0 = ex2(a0);
+          a1 = ex2(a1);
+          a2 = ex2(a2);
+          a3 = ex2(a3);
           if (need_mask) {
             if (!key_ok || q0 < qmin) a0 = 0.f;
             if (!key_ok || q0 + 1 < qmin) a1 = 0.f;
@@ -344,10 +348,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
           const float4 dl = del4[e4];
           const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
           const float2 p01 = unpack2<BF16>(pk[e4 * 2]), p23 = unpack2<BF16>(pk[e4 * 2 + 1]);
-          ds[e4 * 2] =
-              pack2<BF16>(p01.x * (__uint_as_float(src[0]) - dl.x), p01.y * (__uint_as_float(src[1]) - dl.y));
-          ds[e4 * 2 + 1] =
-              pack2<BF16>(p23.x * (__uint_as_float(src[2]) - dl.z), p23.y * (__uint_as_float(src[3]) - dl.w));
+          float d0, d1, d2, d3;  // dS = P (dP - Delta), two lanes per instruction
+          f2_split(mul_f2(f2(p01.x, p01.y),
+                          sub_f2(f2(__uint_as_float(src[0]), __uint_as_float(src[1])), f2(dl.x, dl.y))), d0, d1);
+          f2_split(mul_f2(f2(p23.x, p23.y),
+                          sub_f2(f2(__uint_as_float(src[2]), __uint_as_float(src[3])), f2(dl.z, dl.w))), d2, d3);
+          ds[e4 * 2] = pack2<BF16>(d0, d1);
+          ds[e4 * 2 + 1] = pack2<BF16>(d2, d3);
         }
       }
       tmem_st32(tDP, ds);
@@ -587,7 +594,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t cb = static_cast<uint32_t>(w * 64);
     const long long rowi = static_cast<long long>(bh) * p.S_pad + qrow;
-    const float lse2 = p.lse2[rowi], dlt = p.delta[rowi];
+    const float nlse2 = p.nlse2[rowi], dlt = p.delta[rowi];
     const float sl2 = p.scale_log2;
     bool ok = true;
     for (int j = 0; j < nb; ++j) {
@@ -606,10 +613,10 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
         wait_ld_dep32(v1);
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          pv[c] = ex2(fmaf(__uint_as_float(v0[c]), sl2, -lse2));
-          pv[c + 1] = ex2(fmaf(__uint_as_float(v0[c + 1]), sl2, -lse2));
-          pv[32 + c] = ex2(fmaf(__uint_as_float(v1[c]), sl2, -lse2));
-          pv[32 + c + 1] = ex2(fmaf(__uint_as_float(v1[c + 1]), sl2, -lse2));
+          pv[c] = ex2(fmaf(__uint_as_float(v0[c]), sl2, nlse2));
+          pv[c + 1] = ex2(fmaf(__uint_as_float(v0[c + 1]), sl2, nlse2));
+          pv[32 + c] = ex2(fmaf(__uint_as_float(v1[c]), sl2, nlse2));
+          pv[32 + c + 1] = ex2(fmaf(__uint_as_float(v1[c + 1]), sl2, nlse2));
         }
         if (lim < 64) {
 #pragma unroll

@@ -18,6 +18,10 @@
 #include "tkb_common.cuh"
 #include "tkb_internal.h"
 
+#ifndef TKB_FWD_EMU
+#define TKB_FWD_EMU 0
+#endif
+
 namespace tkb {
 
 template <int D>
@@ -48,7 +52,7 @@ TKB_DEVFN void wait_ld_dep(uint32_t (&r)[32]) {
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __maxnreg__(200) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -262,11 +266,11 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       }
       float mx0 = sv[0], mx1 = sv[1], mx2 = sv[2], mx3 = sv[3];
 #pragma unroll
-      for (int c = 4; c < 128; c += 4) {
-        mx0 = fmaxf(mx0, sv[c]);
-        mx1 = fmaxf(mx1, sv[c + 1]);
-        mx2 = fmaxf(mx2, sv[c + 2]);
-        mx3 = fmaxf(mx3, sv[c + 3]);
+      for (int c = 4; c < 128; c += 8) {
+        mx0 = fmax3(mx0, sv[c], sv[c + 1]);
+        mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
+        mx2 = fmax3(mx2, sv[c + 4], sv[c + 5]);
+        mx3 = fmax3(mx3, sv[c + 6], sv[c + 7]);
       }
       const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
       if (j == 0) {
@@ -286,32 +290,40 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         }
         m_used = mx;
       }
-      const float nm = -m_used;
+      const uint64_t sl2x2 = f2(sl2, sl2), nmx2 = f2(-m_used, -m_used);
       uint32_t pk0[32], pk1[32];
-      float ls0 = 0.f, ls1 = 0.f;
+      uint64_t ls0 = f2(0.f, 0.f), ls1 = f2(0.f, 0.f);
+      // exponentials of keys 2i, 2i+1 (pair i of the half at sv + base): the
+      // scale and the row sums in packed f32x2 instructions; TKB_FWD_EMU of
+      // every 32 pairs on the FMA pipe by the polynomial, the rest on MUFU
+      auto exp_pair = [&](int base, int i, uint32_t& pk, uint64_t& ls) {
+        float x0, x1, a, c;
+        f2_split(fma_f2(f2(sv[base + 2 * i], sv[base + 2 * i + 1]), sl2x2, nmx2), x0, x1);
+        if ((i * TKB_FWD_EMU) % 32 + TKB_FWD_EMU >= 32) {
+          ex2_poly_f2(x0, x1, a, c);
+        } else {
+          a = ex2(x0);
+          c = ex2(x1);
+        }
+        ls = add_f2(ls, f2(a, c));
+        pk = pack2<BF16>(a, c);
+      };
       // P for keys 0-63 goes to TMEM first so that the P*V MMA can start on
       // that half while the exponentials of keys 64-127 are computed.
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = ex2(fmaf(sv[2 * i], sl2, nm));
-        const float c = ex2(fmaf(sv[2 * i + 1], sl2, nm));
-        ls0 += a;
-        ls1 += c;
-        pk0[i] = pack2<BF16>(a, c);
-      }
+      for (int i = 0; i < 32; ++i) exp_pair(0, i, pk0[i], (i & 1) ? ls1 : ls0);
       tmem_st32(tS + 0, pk0);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_ready[2 * w]);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = ex2(fmaf(sv[64 + 2 * i], sl2, nm));
-        const float c = ex2(fmaf(sv[64 + 2 * i + 1], sl2, nm));
-        ls0 += a;
-        ls1 += c;
-        pk1[i] = pack2<BF16>(a, c);
+      for (int i = 0; i < 32; ++i) exp_pair(64, i, pk1[i], (i & 1) ? ls1 : ls0);
+      {
+        float a0, a1, b0, b1;
+        f2_split(ls0, a0, a1);
+        f2_split(ls1, b0, b1);
+        l += (a0 + b0) + (a1 + b1);
       }
-      l += ls0 + ls1;
       tmem_st32(tS + 32, pk1);
       tmem_wait_st();
       tc_fence_before();

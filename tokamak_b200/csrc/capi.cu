@@ -192,11 +192,11 @@ int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const f
   const int S_pad = (S + 127) / 128 * 128;
   const size_t rows = static_cast<size_t>(B) * Hq * S_pad;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  float* lse2 = reinterpret_cast<float*>(ws);
+  float* nlse2 = reinterpret_cast<float*>(ws);
   float* delta = reinterpret_cast<float*>(ws + round256(rows * 4));
   const long long ld = static_cast<long long>(Hq + 2 * Hkv) * D, ldo = static_cast<long long>(Hq) * D;
 
-  cudaError_t e = attn_bwd_pre(out, dout, lse, lse2, delta, ldo, ldo * S, B, S, S_pad, Hq, D, bf16, st);
+  cudaError_t e = attn_bwd_pre(out, dout, lse, nlse2, delta, ldo, ldo * S, B, S, S_pad, Hq, D, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "tkb_gqa_attn_bwd: preprocess", 0);
 
   BwdParams p;
@@ -211,7 +211,7 @@ int tkb_gqa_attn_bwd(const void* qkv, const void* out, const void* dout, const f
                        B, ld, ld * S);
   if (e == cudaSuccess) e = make_tmap_rows(&p.tmdO, dout, bf16, ldo, S, B, ldo, ldo * S);
   if (e != cudaSuccess) return cuda_status(e, "tkb_gqa_attn_bwd: tensor map", 0);
-  p.lse2 = lse2;
+  p.nlse2 = nlse2;
   p.delta = delta;
   uint16_t* dbase = static_cast<uint16_t*>(dqkv);
   p.dq = dbase;

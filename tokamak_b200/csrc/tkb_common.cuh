@@ -374,6 +374,65 @@ TKB_DEVFN float lg2(float x) {
   return y;
 }
 
+// Three-input maximum (one instruction on sm_100).
+TKB_DEVFN float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two fp32 lanes in one 64-bit register pair (lo in bits 0-31), operated on by
+// the packed f32x2 instructions of sm_100: one issue slot for two results.
+TKB_DEVFN uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+TKB_DEVFN void f2_split(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+TKB_DEVFN uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+TKB_DEVFN uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+TKB_DEVFN uint64_t mul_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+TKB_DEVFN uint64_t sub_f2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x of two lanes on the FMA pipe (no MUFU): x = n + f with n = rint(x) taken
+// from the low mantissa bits of x + 1.5*2^23, f in [-1/2, 1/2]; 2^f by a
+// degree-3 polynomial with p(0) = 1 fitted here (Lawson-reweighted least
+// squares on Chebyshev nodes) to a relative error of 1.02e-4, below half an
+// ulp of bf16 (2^-9) and of f16 (2^-11); the result is p with n added to its
+// exponent field.  Inputs are clamped at -125 so that the exponent stays
+// normal: 2^-125 in place of a smaller value or of 0 (a masked -inf) is
+// below 1e-37 in a sum whose largest term is at least 1.
+TKB_DEVFN void ex2_poly_f2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t x = f2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t magic = f2(12582912.f, 12582912.f);
+  const uint64_t t = add_f2(x, magic);
+  const uint64_t f = sub_f2(x, sub_f2(t, magic));
+  uint64_t p = fma_f2(f2(0.05500893f, 0.05500893f), f, f2(0.24221095f, 0.24221095f));
+  p = fma_f2(p, f, f2(0.6932829f, 0.6932829f));
+  p = fma_f2(p, f, f2(1.f, 1.f));
+  float p0, p1, t0, t1;
+  f2_split(p, p0, p1);
+  f2_split(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
 // Pack two floats into one 32-bit word of 16-bit values, lo in bits 0-15.
 template <bool BF16>
 TKB_DEVFN uint32_t pack2(float lo, float hi) {

@@ -27,7 +27,7 @@ struct alignas(64) BwdParams {
   CUtensorMap tmQ, tmK, tmV, tmdO;
   uint16_t* ds;               // null: dQ recomputes S and dP; else dS tiles (see ds_tile)
   long long ds_tiles;         // dS tiles per (batch, q head)
-  const float* lse2;          // [B*Hq][S_pad]  LSE * log2(e), +inf on padded rows
+  const float* nlse2;         // [B*Hq][S_pad]  -LSE * log2(e), -inf on padded rows
   const float* delta;         // [B*Hq][S_pad]  rowsum(O * dO), 0 on padded rows
   void* dq;                   // row-major, dkv_row_stride elements per row, head h at h*D
   void* dk;                   // row-major, dkv_row_stride elements per row, head g at g*D

@@ -118,7 +118,9 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
     /* measured: prefetching the next row pays for elementwise groups (twin
      * 0.69 -> 0.76, bias 0.82 -> 0.91 of HBM) but costs a normalisation the
      * resident blocks that its row reduction needs (0.65 -> 0.60) */
-    o->persist = !group_has_norm(g, pg) && !pg->is_qkv_prep; /* the QKV prep forward is one row block per block */
+    /* the QKV prep's normalisation is per 64-wide head, within a warp: it
+     * needs no block-wide reduction and its forward is persistent too */
+    o->persist = !group_has_norm(g, pg) || pg->is_qkv_prep;
 }
 
 void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *o) {
@@ -1308,40 +1310,78 @@ static void emit_qkv_prep(Em *e) {
     bprintf(b, "#define TKG_HD2 %d\n#define TKG_QK2 %d\n#define TKG_SEQ %d\n#define TKG_CPH (TKG_HD2 / TKG_VP)\n", hd2, qk2,
             S > 0 ? S : 1);
 
+    /* forward: persistent over row blocks; the next row block's inputs and
+     * cos/sin pairs are requested before the current one is computed, the
+     * per-channel bias and gains are loaded once */
     set_args(e, 0);
-    kernel_head(e, "fwd", 1);
-    bprintf(b, "  const int pos = row %% TKG_SEQ; (void)pos;\n");
-    load_array(b, "tx", A(e, KA_IN, -1, 0), "TKG_C2", "0");
-    pairs_begin(b);
-    bprintf(b, "          const float2 bb = %s[tid]; tx[k][q].x += bb.x; tx[k][q].y += bb.y;\n", A(e, KA_PARAM, n->id, 2));
-    pairs_end(b);
+    kernel_head(e, "fwd", 0);
+    bprintf(b, "  float2 tqb[TKG_KCH][TKG_VP], tqg[TKG_KCH][TKG_VP];\n"
+               "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\n"
+               "    const int tkm_ch = tkm_lr + k * TKG_TPR;\n"
+               "    _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+               "      tqb[k][q] = tkm_ch < TKG_NCH ? __ldg(&%s[tkm_ch * TKG_VP + q]) : make_float2(0.f, 0.f);\n",
+            A(e, KA_PARAM, n->id, 2));
+    if (n->has_qknorm)
+        bprintf(b, "      tqg[k][q] = (tkm_ch < TKG_NCH && tkm_ch * TKG_VP < TKG_QK2) ? __ldg(&%s[tkm_ch * TKG_VP + q])"
+                   " : make_float2(1.f, 1.f);\n",
+                A(e, KA_PARAM, n->id, 0));
+    else
+        bprintf(b, "      tqg[k][q] = make_float2(1.f, 1.f);\n");
+    bprintf(b, "    }\n  }\n"
+               "  float2 tx_nx[TKG_KCH][TKG_VP], tcs_nx[TKG_KCH][TKG_VP];\n"
+               "  int tkm_rb = blockIdx.x;\n"
+               "#define TKM_QKV_NEXT(rbv) {\\\n"
+               "    const int rown = (rbv) * TKG_RPB + threadIdx.x / TKG_TPR;\\\n"
+               "    const bool okn = (rbv) < TKG_NRB && rown < TKG_ROWS;\\\n"
+               "    const int posn = rown %% TKG_SEQ; (void)posn;\\\n"
+               "    _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\\\n"
+               "      const int tkm_ch = tkm_lr + k * TKG_TPR;\\\n"
+               "      if (okn && tkm_ch < TKG_NCH) tkm_ld<TKG_VP>(%s, (long long)rown * TKG_C2 + tkm_ch * TKG_VP, tx_nx[k]);\\\n"
+               "      else tkm_zero<TKG_VP>(tx_nx[k]);\\\n"
+               "      _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\\\n"
+               "        const int tid = tkm_ch * TKG_VP + q;\\\n",
+            A(e, KA_IN, -1, 0));
+    if (n->has_rope)
+        bprintf(b, "        tcs_nx[k][q] = (okn && tkm_ch < TKG_NCH && tid < TKG_QK2)"
+                   " ? __ldg(&%s[(size_t)posn * TKG_HD2 + (tid %% TKG_HD2)]) : make_float2(1.f, 0.f);\\\n",
+                A(e, KA_ROPE, -1, 0));
+    else
+        bprintf(b, "        tcs_nx[k][q] = make_float2(1.f, 0.f); (void)tid;\\\n");
+    bprintf(b, "      }\\\n    }\\\n  }\n"
+               "  TKM_QKV_NEXT(tkm_rb)\n"
+               "  for (; tkm_rb < TKG_NRB; tkm_rb += gridDim.x) {\n"
+               "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
+               "  const bool tkm_row_ok = row < TKG_ROWS;\n");
+    decl_array(b, "tx");
+    decl_array(b, "tcs");
+    copy_array(b, "tx", "tx_nx");
+    copy_array(b, "tcs", "tcs_nx");
+    bprintf(b, "  TKM_QKV_NEXT(tkm_rb + gridDim.x)\n"
+               "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\n"
+               "    const int tkm_ch = tkm_lr + k * TKG_TPR;\n"
+               "    float ss = 0.f;\n"
+               "    _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+               "      tx[k][q].x += tqb[k][q].x; tx[k][q].y += tqb[k][q].y;\n"
+               "      ss += tx[k][q].x * tx[k][q].x + tx[k][q].y * tx[k][q].y;\n"
+               "    }\n");
     if (n->has_qknorm) {
-        bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) {\n"
-                   "    const int tkm_ch = tkm_lr + k * TKG_TPR;\n"
-                   "    float ss = 0.f;\n"
-                   "    _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) ss += tx[k][q].x * tx[k][q].x + tx[k][q].y * tx[k][q].y;\n"
-                   "    const float istd = rsqrtf(tkm_group_sum<TKG_CPH>(ss) * ");
+        bprintf(b, "    const float istd = rsqrtf(tkm_group_sum<TKG_CPH>(ss) * ");
         emit_float(b, 1.0 / n->head_dim);
         bprintf(b, " + 1e-5f);\n"
-                   "    if (tkm_row_ok && tkm_ch < TKG_NCH && tkm_ch * TKG_VP < TKG_QK2) {\n"
-                   "      _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
-                   "        const float2 gm = %s[tkm_ch * TKG_VP + q];\n"
-                   "        tx[k][q] = make_float2(tx[k][q].x * istd * gm.x, tx[k][q].y * istd * gm.y);\n"
-                   "      }\n    }\n  }\n",
-                A(e, KA_PARAM, n->id, 0));
+                   "    const bool tkm_qk = tkm_ch * TKG_VP < TKG_QK2;\n"
+                   "    _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) if (tkm_qk)\n"
+                   "      tx[k][q] = make_float2(tx[k][q].x * istd * tqg[k][q].x, tx[k][q].y * istd * tqg[k][q].y);\n");
+    } else {
+        bprintf(b, "    (void)ss; (void)tkm_ch; (void)tqg;\n");
     }
-    if (n->has_rope) {
-        pairs_begin(b);
-        bprintf(b, "          if (tid < TKG_QK2) {\n"
-                   "            const float2 cs = %s[(size_t)pos * TKG_HD2 + (tid %% TKG_HD2)];\n"
-                   "            const float2 v = tx[k][q];\n"
-                   "            tx[k][q] = make_float2(v.x * cs.x - v.y * cs.y, v.x * cs.y + v.y * cs.x);\n"
-                   "          }\n",
-                A(e, KA_ROPE, -1, 0));
-        pairs_end(b);
-    }
+    if (n->has_rope)
+        bprintf(b, "    _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q) {\n"
+                   "      const float2 v = tx[k][q], cs = tcs[k][q];\n"
+                   "      tx[k][q] = make_float2(v.x * cs.x - v.y * cs.y, v.x * cs.y + v.y * cs.x);\n"
+                   "    }\n");
+    bprintf(b, "  }\n");
     store_array(b, A(e, KA_OUT, -1, 0), "TKG_C2", "0", "tx", 0);
-    bprintf(b, "}\n\n");
+    bprintf(b, "  }\n#undef TKM_QKV_NEXT\n}\n\n");
 
     set_args(e, 1);
     kernel_head(e, "bwd", 0);

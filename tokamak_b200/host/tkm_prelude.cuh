@@ -461,21 +461,56 @@ extern "C" __global__ void __launch_bounds__(256) tkm_act_to_f32(const tkm_act_t
   }
 }
 
-// fp32 -> bf16 copies of GEMM weights after a load
-extern "C" __global__ void __launch_bounds__(256) tkm_f32_to_bf16(const float* __restrict__ src, uint16_t* __restrict__ dst,
-                                                                  long long n) {
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
-    const uint32_t u = __float_as_uint(src[i]);
-    const uint32_t r = ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) ? (u | 0x400000u)
-                                                                              : u + 0x7FFFu + ((u >> 16) & 1u);
-    dst[i] = (uint16_t)(r >> 16);
-  }
+// fp32 -> bf16, round to nearest even (NaN kept quiet): GEMM weights after a
+// load, and gradients onto the bf16 all-reduce wire
+__device__ __forceinline__ uint32_t tkm_bf16_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  const uint32_t r = ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) ? (u | 0x400000u)
+                                                                          : u + 0x7FFFu + ((u >> 16) & 1u);
+  return r >> 16;
 }
 
-// bf16 -> fp32 (gradients coming back from a bf16 all-reduce)
+// Eight values per thread and step (two 16-byte loads, one 16-byte store)
+// when both pointers are 16-byte aligned, the rest one by one.
+extern "C" __global__ void __launch_bounds__(256) tkm_f32_to_bf16(const float* __restrict__ src, uint16_t* __restrict__ dst,
+                                                                  long long n) {
+  const long long stride = (long long)gridDim.x * 256;
+  long long done = 0;
+  if ((((uint64_t)src | (uint64_t)dst) & 15) == 0) {
+    const long long n8 = n >> 3;
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n8; i += stride) {
+      const float4 a = reinterpret_cast<const float4*>(src)[2 * i], b = reinterpret_cast<const float4*>(src)[2 * i + 1];
+      uint4 o;
+      o.x = tkm_bf16_bits(a.x) | (tkm_bf16_bits(a.y) << 16);
+      o.y = tkm_bf16_bits(a.z) | (tkm_bf16_bits(a.w) << 16);
+      o.z = tkm_bf16_bits(b.x) | (tkm_bf16_bits(b.y) << 16);
+      o.w = tkm_bf16_bits(b.z) | (tkm_bf16_bits(b.w) << 16);
+      reinterpret_cast<uint4*>(dst)[i] = o;
+    }
+    done = n8 << 3;
+  }
+  for (long long i = done + blockIdx.x * 256ll + threadIdx.x; i < n; i += stride) dst[i] = (uint16_t)tkm_bf16_bits(src[i]);
+}
+
+// bf16 -> fp32 (gradients coming back from a bf16 all-reduce), vectorised as above
 extern "C" __global__ void __launch_bounds__(256) tkm_bf16_to_f32(const uint16_t* __restrict__ src, float* __restrict__ dst,
                                                                   long long n) {
-  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256)
+  const long long stride = (long long)gridDim.x * 256;
+  long long done = 0;
+  if ((((uint64_t)src | (uint64_t)dst) & 15) == 0) {
+    const long long n8 = n >> 3;
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n8; i += stride) {
+      const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+      reinterpret_cast<float4*>(dst)[2 * i] =
+          make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xFFFF0000u), __uint_as_float(v.y << 16),
+                      __uint_as_float(v.y & 0xFFFF0000u));
+      reinterpret_cast<float4*>(dst)[2 * i + 1] =
+          make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xFFFF0000u), __uint_as_float(v.w << 16),
+                      __uint_as_float(v.w & 0xFFFF0000u));
+    }
+    done = n8 << 3;
+  }
+  for (long long i = done + blockIdx.x * 256ll + threadIdx.x; i < n; i += stride)
     dst[i] = __uint_as_float((uint32_t)src[i] << 16);
 }
 
