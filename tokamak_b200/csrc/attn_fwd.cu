@@ -52,7 +52,7 @@ TKB_DEVFN void wait_ld_dep(uint32_t (&r)[32]) {
 }
 
 template <int D, bool BF16>
-__global__ void __maxnreg__(200) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
