@@ -153,6 +153,36 @@ def test_softmax_loss(rng, dtype, kind, rows, C):
     assert corr.item() == rcorr
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("kind", [0, 1, 2])
+@pytest.mark.parametrize("rows,C", [(300, 8200), (7, 32768), (160, 16392)])
+def test_softmax_loss_wide_rows_ties(rng, dtype, kind, rows, C):
+    """16-bit vocabulary rows (8192 to 32768 wide, ragged against the
+    kernel's 4096-element strides, more rows than resident blocks): rows
+    whose maximum occurs twice count as correct only for the first index,
+    a label on the second occurrence does not."""
+    o = ops()
+    x, xn = dev(2 * rng.standard_normal((rows, C)), dtype)
+    lab = rng.integers(0, C, rows).astype(np.int32)
+    host = x.float().cpu().numpy()
+    for r in range(0, rows, 3):
+        i, j = sorted(rng.choice(C, 2, replace=False))
+        host[r, i] = host[r, j] = 20.0
+        lab[r] = i if r % 2 == 0 else j
+    x = torch.from_numpy(host).to(dtype).cuda()
+    xn = x.float().cpu().numpy()
+    tl = torch.from_numpy(lab).cuda()
+    loss, dl, corr = o.softmax_loss(x, tl, kind, 2.0)
+    rloss, rdl, rcorr = oracle.softmax_loss(xn, lab, kind, 2.0)
+    assert abs(loss.item() - rloss) <= 1e-5 + 1e-2 * abs(rloss)
+    got = dl.float().cpu().numpy()
+    if dtype == torch.float16 and kind == 2:
+        assert np.abs(got - rdl).max() <= 1e-7 + 1e-2 * np.abs(rdl).max()
+    else:
+        assert rel_l2(got, rdl) < tol(dtype)
+    assert corr.item() == rcorr
+
+
 def test_sgd(rng):
     o = ops()
     n1, n2 = 1000, 37

@@ -273,21 +273,16 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         mx3 = fmax3(mx3, sv[c + 6], sv[c + 7]);
       }
       const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      // Raise the running max when this block's exceeds it by more than 8
+      // (2^8 headroom in fp32): the row sum now, the partial O row below,
+      // after the first half's exponentials, when half of S is no longer
+      // live in registers (the O chunks then fit without spilling).
+      float resc = 0.f;
       if (j == 0) {
         m_used = (mx == -INFINITY) ? 0.f : mx;
       } else if (mx > m_used + 8.0f) {
-        // Raise the running max: rescale the partial O row and the row sum.
-        const float f = ex2(m_used - mx);
-        l *= f;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          wait_ld_dep(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-          tmem_st32(tO + c * 32, o);
-        }
+        resc = ex2(m_used - mx);
+        l *= resc;
         m_used = mx;
       }
       const uint64_t sl2x2 = f2(sl2, sl2), nmx2 = f2(-m_used, -m_used);
@@ -306,12 +301,25 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           c = ex2(x1);
         }
         ls = add_f2(ls, f2(a, c));
-        pk = pack2<BF16>(a, c);
+        pk = pack2_int<BF16>(a, c);
       };
       // P for keys 0-63 goes to TMEM first so that the P*V MMA can start on
       // that half while the exponentials of keys 64-127 are computed.
 #pragma unroll
       for (int i = 0; i < 32; ++i) exp_pair(0, i, pk0[i], (i & 1) ? ls1 : ls0);
+      if (resc != 0.f) {
+        // O of the previous blocks is complete: s_full of this block was
+        // committed after their P*V MMAs.  P*V of this block waits for p_ready.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          wait_ld_dep(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * resc);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
       tmem_st32(tS + 0, pk0);
       tmem_wait_st();
       tc_fence_before();

@@ -154,6 +154,20 @@ TKB_DEVFN void st_global_hint(void* gaddr, uint4 v, uint64_t cache_policy) {
                : "memory");
 }
 
+// 16-byte streaming accesses: a load that does not allocate in L1 (read-only
+// data), a store marked evict-first (written once, not read back soon).
+TKB_DEVFN uint4 ld_stream_v4(const uint4* gaddr) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(gaddr));
+  return r;
+}
+TKB_DEVFN void st_stream_v4(uint4* gaddr, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(gaddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 TKB_DEVFN uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -443,6 +457,27 @@ TKB_DEVFN uint32_t pack2(float lo, float hi) {
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   }
   return r;
+}
+
+// The same pack kept off the XU pipe.  The f32 -> bf16x2 conversion issues
+// on the XU pipe, as ex2 does, and the attention forward's softmax phase
+// keeps that pipe 86 % busy (ncu); packing P on the integer pipes made the
+// forward 3-7 % faster (same-box A/B), while the dK/dV kernel, whose integer
+// pipe is busier, ran 2-5 % slower with it and keeps cvt.  For bf16 this
+// rounds on the integer pipes: add half of the dropped
+// range (0x8000) to each float's bits and keep the high halves (one byte
+// permute per pair).  That is round-to-nearest with ties away from zero in
+// magnitude; it differs from cvt.rn only when the dropped 16 bits are
+// exactly 0x8000 and the kept part is even (1 in 65536 of arbitrary values),
+// by one bf16 ulp.  Finite inputs only (P in [0, 1]).  f16 keeps cvt.rn.
+template <bool BF16>
+TKB_DEVFN uint32_t pack2_int(float lo, float hi) {
+  if constexpr (BF16) {
+    const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
+    return __byte_perm(a, b, 0x7632);
+  } else {
+    return pack2<false>(lo, hi);
+  }
 }
 template <bool BF16>
 TKB_DEVFN float2 unpack2(uint32_t v) {
