@@ -30,6 +30,14 @@
 #include "tkb_common.cuh"
 #include "tkb_internal.h"
 
+// Groups of four exponentials (of 16 per thread and step) that the dK/dV
+// kernel computes with the FMA-pipe polynomial instead of ex2.  Same-box
+// A/B at the headline shape: 2 and 4 groups within noise of none (backward
+// 1.664-1.677 vs 1.650-1.671 ms), 8 groups slower (1.689-1.694); off.
+#ifndef TKB_BWD_EMU
+#define TKB_BWD_EMU 0
+#endif
+
 namespace tkb {
 
 TKB_DEVFN void wait_ld_dep32(uint32_t (&r)[32]) {
@@ -315,10 +323,15 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
           float a0, a1, a2, a3;
           f2_split(fma_f2(f2(__uint_as_float(src[0]), __uint_as_float(src[1])), sl2x2, f2(l.x, l.y)), a0, a1);
           f2_split(fma_f2(f2(__uint_as_float(src[2]), __uint_as_float(src[3])), sl2x2, f2(l.z, l.w)), a2, a3);
-          a0 = ex2(a0);
-          a1 = ex2(a1);
-          a2 = ex2(a2);
-          a3 = ex2(a3);
+          if ((e4 * TKB_BWD_EMU) % 16 + TKB_BWD_EMU >= 16) {
+            ex2_poly_f2(a0, a1, a0, a1);
+            ex2_poly_f2(a2, a3, a2, a3);
+          } else {
+            a0 = ex2(a0);
+            a1 = ex2(a1);
+            a2 = ex2(a2);
+            a3 = ex2(a3);
+          }
           if (need_mask) {
             if (!key_ok || q0 < qmin) a0 = 0.f;
             if (!key_ok || q0 + 1 < qmin) a1 = 0.f;

@@ -9,7 +9,7 @@
 // 128-key K/V blocks of the matching kv head through shared memory.
 //   warps 0-3  softmax warpgroup for query tile 0 (thread = query row)
 //   warps 4-7  softmax warpgroup for query tile 1
-//   warp 8     TMA producer (Q once, K/V ring of NST stages)
+//   warp 8     TMA producer (Q once, K and V rings of NSTK / NSTV stages)
 //   warp 9     tcgen05 MMA issuer, TMEM owner
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // The softmax warps overwrite the first 64 columns of S with P (16-bit pairs),
@@ -21,6 +21,16 @@
 #ifndef TKB_FWD_EMU
 #define TKB_FWD_EMU 0
 #endif
+// V stages at D = 128 (2 or 3) and heads per CTA group (0: all heads'
+// query-tile pairs longest first).  Same-box A/B at the headline shape:
+// forward 0.624 ms with (2, 0), 0.633 with (3, 0), 0.601 with (2, 4),
+// 0.559 with (2, 8), 0.567 with (2, 16), 0.566 with (3, 8).
+#ifndef TKB_FWD_NSTV
+#define TKB_FWD_NSTV 2
+#endif
+#ifndef TKB_FWD_HG
+#define TKB_FWD_HG 8
+#endif
 
 namespace tkb {
 
@@ -28,15 +38,20 @@ template <int D>
 struct FwdCfg {
   static constexpr int TILE = 128 * D * 2;  // bytes of one 128-row x D tile
   static constexpr int SLAB = 128 * 128;    // bytes of one 64-column swizzle slab
-  static constexpr int NST = (D == 64) ? 4 : 2;
+  // K and V rings counted apart: at D = 128 a third V stage (224 KB of tiles
+  // in all) fits beside two K stages; it measured no faster once the CTAs of
+  // a head group read K/V from L2.
+  static constexpr int NSTK = (D == 64) ? 4 : 2;
+  static constexpr int NSTV = (D == 64) ? 4 : TKB_FWD_NSTV;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + 2 * TILE;
-  static constexpr int OFF_V = OFF_K + NST * TILE;
-  static constexpr int OFF_BAR = OFF_V + NST * TILE;
-  // q_full, k_full[NST], k_empty[NST], v_full[NST], v_empty[NST], s_full[2], p_ready[2][2], o_done[2], drain
-  static constexpr int NBAR = 1 + 4 * NST + 9;
+  static constexpr int OFF_V = OFF_K + NSTK * TILE;
+  static constexpr int OFF_BAR = OFF_V + NSTV * TILE;
+  // q_full, k_full[NSTK], k_empty[NSTK], v_full[NSTV], v_empty[NSTV], s_full[2], p_ready[2][2], o_done[2], drain
+  static constexpr int NBAR = 1 + 2 * NSTK + 2 * NSTV + 9;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + slack for 1024-byte alignment
+  static_assert(SMEM <= 232448, "forward tiles exceed 227 KB of shared memory");
   static constexpr uint32_t TM_S0 = 0, TM_S1 = 128, TM_O0 = 256, TM_O1 = 256 + D;
 };
 
@@ -51,6 +66,28 @@ TKB_DEVFN void wait_ld_dep(uint32_t (&r)[32]) {
                : "memory");
 }
 
+// CTA -> (batch x q head bh, query-tile pair t).  Heads go in groups of hg,
+// longest pair first inside a group (causal), so that the CTAs running at
+// the same time read the K/V tiles of a few heads, which then come from L2;
+// hg = 0 orders all heads' pairs longest first.
+TKB_DEVFN void fwd_cta_order(int cta, int BH, int npairs, int hg, int& bh, int& t) {
+  if (hg <= 0) {
+    bh = cta % BH;
+    t = npairs - 1 - cta / BH;
+    return;
+  }
+  const int full = BH / hg, per = hg * npairs;
+  if (cta < full * per) {
+    const int r = cta % per;
+    t = npairs - 1 - r / hg;
+    bh = (cta / per) * hg + r % hg;
+  } else {
+    const int hr = BH - full * hg, r = cta - full * per;
+    t = npairs - 1 - r / hr;
+    bh = full * hg + r % hr;
+  }
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
@@ -60,10 +97,10 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + C::NST;
-  uint64_t* v_full = k_empty + C::NST;
-  uint64_t* v_empty = v_full + C::NST;
-  uint64_t* s_full = v_empty + C::NST;
+  uint64_t* k_empty = k_full + C::NSTK;
+  uint64_t* v_full = k_empty + C::NSTK;
+  uint64_t* v_empty = v_full + C::NSTV;
+  uint64_t* s_full = v_empty + C::NSTV;
   uint64_t* p_ready = s_full + 2;  // [w][half]: P of keys 0-63 / 64-127 of the block is in TMEM
   uint64_t* o_done = p_ready + 4;
   uint64_t* mma_drain = o_done + 2;
@@ -72,8 +109,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
 
   const int warp = warp_id(), lane = lane_id();
   const int BH = p.B * p.Hq;
-  const int bh = blockIdx.x % BH;
-  const int t = p.n_pairs - 1 - static_cast<int>(blockIdx.x / BH);  // longest (causal) first
+  int bh, t;  // (batch, q head), query-tile pair
+  fwd_cta_order(blockIdx.x, BH, p.n_pairs, TKB_FWD_HG, bh, t);
   const int b = bh / p.Hq, h = bh % p.Hq;
   const int g = h / (p.Hq / p.Hkv);
   const int nkv = (p.S + 127) >> 7;
@@ -87,9 +124,11 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < C::NST; ++s) {
+    for (int s = 0; s < C::NSTK; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::NSTV; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
@@ -128,22 +167,21 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
                       (2 * t + w) * 128, b, pol_q);
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
-        const int s = j % C::NST;
-        const uint32_t ph = (j / C::NST) & 1;
-        if (!mbar_wait(&k_empty[s], ph ^ 1, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[s], C::TILE);
+        const int sk = j % C::NSTK, sv = j % C::NSTV;
+        if (!mbar_wait(&k_empty[sk], ((j / C::NSTK) & 1) ^ 1, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[sk], C::TILE);
 #pragma unroll
         for (int hh = 0; hh < D / 64; ++hh)
-          tma_load_3d(smem + C::OFF_K + s * C::TILE + hh * C::SLAB, &p.tmK, &k_full[s], g * D + hh * 64,
+          tma_load_3d(smem + C::OFF_K + sk * C::TILE + hh * C::SLAB, &p.tmK, &k_full[sk], g * D + hh * 64,
                       j * 128, b, pol_kv);
-        if (!mbar_wait(&v_empty[s], ph ^ 1, abort_flag)) {
+        if (!mbar_wait(&v_empty[sv], ((j / C::NSTV) & 1) ^ 1, abort_flag)) {
           issued = -(j + 1);  // K of block j is in flight, V is not
           break;
         }
-        mbar_arrive_expect_tx(&v_full[s], C::TILE);
+        mbar_arrive_expect_tx(&v_full[sv], C::TILE);
 #pragma unroll
         for (int hh = 0; hh < D / 64; ++hh)
-          tma_load_3d(smem + C::OFF_V + s * C::TILE + hh * C::SLAB, &p.tmV, &v_full[s], g * D + hh * 64,
+          tma_load_3d(smem + C::OFF_V + sv * C::TILE + hh * C::SLAB, &p.tmV, &v_full[sv], g * D + hh * 64,
                       j * 128, b, pol_kv);
         issued = j + 1;
       }
@@ -152,8 +190,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         volatile int never = 0;
         mbar_wait(q_full, 0, &never);
         const int nk = issued < 0 ? -issued : issued, nv = issued < 0 ? -issued - 1 : issued;
-        for (int j = max(0, nk - C::NST); j < nk; ++j) mbar_wait(&k_full[j % C::NST], (j / C::NST) & 1, &never);
-        for (int j = max(0, nv - C::NST); j < nv; ++j) mbar_wait(&v_full[j % C::NST], (j / C::NST) & 1, &never);
+        for (int j = max(0, nk - C::NSTK); j < nk; ++j) mbar_wait(&k_full[j % C::NSTK], (j / C::NSTK) & 1, &never);
+        for (int j = max(0, nv - C::NSTV); j < nv; ++j) mbar_wait(&v_full[j % C::NSTV], (j / C::NSTV) & 1, &never);
       }
     }
   } else if (warp == 9) {
@@ -193,8 +231,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
         umma_commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < nblk; ++j) {
-        const int s = j % C::NST, s1 = (j + 1) % C::NST;
-        if (!(ok = mbar_wait(&v_full[s], (j / C::NST) & 1, abort_flag))) break;
+        const int s = j % C::NSTV, s1 = (j + 1) % C::NSTK;  // V stage of block j, K stage of block j + 1
+        if (!(ok = mbar_wait(&v_full[s], (j / C::NSTV) & 1, abort_flag))) break;
         bool k_next = false;
         for (int w = 0; w < 2 && ok; ++w) {
           if (j >= nb[w]) continue;
@@ -207,7 +245,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
           if (j == nb[w] - 1) umma_commit(&o_done[w]);
           if (j + 1 < nb[w]) {
             if (!k_next) {
-              if (!(ok = mbar_wait(&k_full[s1], ((j + 1) / C::NST) & 1, abort_flag))) break;
+              if (!(ok = mbar_wait(&k_full[s1], ((j + 1) / C::NSTK) & 1, abort_flag))) break;
               tc_fence_after();
               k_next = true;
             }
