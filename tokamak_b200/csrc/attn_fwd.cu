@@ -18,9 +18,6 @@
 #include "tkb_common.cuh"
 #include "tkb_internal.h"
 
-#ifndef TKB_FWD_EMU
-#define TKB_FWD_EMU 0
-#endif
 // V stages at D = 128 (2 or 3) and heads per CTA group (0: all heads'
 // query-tile pairs longest first).  Same-box A/B at the headline shape:
 // forward 0.624 ms with (2, 0), 0.633 with (3, 0), 0.601 with (2, 4),
@@ -327,17 +324,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
       uint32_t pk0[32], pk1[32];
       uint64_t ls0 = f2(0.f, 0.f), ls1 = f2(0.f, 0.f);
       // exponentials of keys 2i, 2i+1 (pair i of the half at sv + base): the
-      // scale and the row sums in packed f32x2 instructions; TKB_FWD_EMU of
-      // every 32 pairs on the FMA pipe by the polynomial, the rest on MUFU
+      // scale and the row sums in packed f32x2 instructions
       auto exp_pair = [&](int base, int i, uint32_t& pk, uint64_t& ls) {
         float x0, x1, a, c;
         f2_split(fma_f2(f2(sv[base + 2 * i], sv[base + 2 * i + 1]), sl2x2, nmx2), x0, x1);
-        if ((i * TKB_FWD_EMU) % 32 + TKB_FWD_EMU >= 32) {
-          ex2_poly_f2(x0, x1, a, c);
-        } else {
-          a = ex2(x0);
-          c = ex2(x1);
-        }
+        a = ex2(x0);
+        c = ex2(x1);
         ls = add_f2(ls, f2(a, c));
         pk = pack2_int<BF16>(a, c);
       };

@@ -12,6 +12,15 @@
 //     reduced by a second kernel (deterministic, no atomics).
 #include "tkb_common.cuh"
 
+// Pairs (of the four in each 16-byte vector) whose exponentials the
+// register-resident softmax loss computes with the FMA-pipe polynomial
+// (ex2_poly_f2, relative error 1.02e-4) instead of ex2, to offload the MUFU
+// unit the kernel keeps busy: same box, 8192 x 32000 bf16, 0.2222 ms with
+// none, 0.2181 with one, 0.2245 with two.
+#ifndef TKB_CE_EMU
+#define TKB_CE_EMU 1
+#endif
+
 namespace tkb {
 
 // ------------------------------------------------------------------ loads
@@ -1132,8 +1141,12 @@ __global__ void __launch_bounds__(512, 1) softmax_loss_reg_kernel(const T* __res
         const float2 f = unpack2<BF>(wv[i]);
         float a, b;
         f2_split(fma_f2(f2(f.x, f.y), l2e2, nml2), a, b);
-        a = ex2(a);  // -inf (padding) -> 0
-        b = ex2(b);
+        if (i < TKB_CE_EMU) {
+          ex2_poly_f2(a, b, a, b);
+        } else {
+          a = ex2(a);  // -inf (padding) -> 0
+          b = ex2(b);
+        }
         ev[k][2 * i] = a;
         ev[k][2 * i + 1] = b;
         const uint64_t ab = f2(a, b);
