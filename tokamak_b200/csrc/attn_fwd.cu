@@ -85,6 +85,107 @@ TKB_DEVFN void fwd_cta_order(int cta, int BH, int npairs, int hg, int& bh, int& 
   }
 }
 
+// One key block of the online softmax for this thread's query row: S from
+// TMEM, the causal and
+// sequence-end masks, the running max raised when this block's exceeds it
+// by more than 8 (rescaling O in TMEM), P written over S in two halves, and
+// release(h) once half h (keys 64h .. 64h+63) is in TMEM.
+template <int D, bool BF16, typename Release>
+TKB_DEVFN void softmax_block(uint32_t tS, uint32_t tO, float sl2, int j, int qt, int qrow, int S, int causal,
+                             float& m_used, float& l, Release&& release) {
+  uint32_t r0[32], r1[32], r2[32], r3[32];
+  tmem_ld32(tS + 0, r0);
+  tmem_ld32(tS + 32, r1);
+  tmem_ld32(tS + 64, r2);
+  tmem_ld32(tS + 96, r3);
+  wait_ld_dep(r0);
+  wait_ld_dep(r1);
+  wait_ld_dep(r2);
+  wait_ld_dep(r3);
+  float sv[128];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    sv[i] = __uint_as_float(r0[i]);
+    sv[32 + i] = __uint_as_float(r1[i]);
+    sv[64 + i] = __uint_as_float(r2[i]);
+    sv[96 + i] = __uint_as_float(r3[i]);
+  }
+  const int kbase = j * 128;
+  if ((causal && kbase + 127 > qt * 128) || kbase + 128 > S) {
+    const int lim = min(S - kbase, causal ? qrow - kbase + 1 : 128);
+#pragma unroll
+    for (int c = 0; c < 128; ++c)
+      if (c >= lim) sv[c] = -INFINITY;
+  }
+  float mx0 = sv[0], mx1 = sv[1], mx2 = sv[2], mx3 = sv[3];
+#pragma unroll
+  for (int c = 4; c < 128; c += 8) {
+    mx0 = fmax3(mx0, sv[c], sv[c + 1]);
+    mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
+    mx2 = fmax3(mx2, sv[c + 4], sv[c + 5]);
+    mx3 = fmax3(mx3, sv[c + 6], sv[c + 7]);
+  }
+  const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+  // Raise the running max when this block's exceeds it by more than 8
+  // (2^8 headroom in fp32): the row sum now, the partial O row below,
+  // after the first half's exponentials, when half of S is no longer
+  // live in registers (the O chunks then fit without spilling).
+  float resc = 0.f;
+  if (j == 0) {
+    m_used = (mx == -INFINITY) ? 0.f : mx;
+  } else if (mx > m_used + 8.0f) {
+    resc = ex2(m_used - mx);
+    l *= resc;
+    m_used = mx;
+  }
+  const uint64_t sl2x2 = f2(sl2, sl2), nmx2 = f2(-m_used, -m_used);
+  uint32_t pk0[32], pk1[32];
+  uint64_t ls0 = f2(0.f, 0.f), ls1 = f2(0.f, 0.f);
+  // exponentials of keys 2i, 2i+1 (pair i of the half at sv + base): the
+  // scale and the row sums in packed f32x2 instructions
+  auto exp_pair = [&](int base, int i, uint32_t& pk, uint64_t& ls) {
+    float x0, x1, a, c;
+    f2_split(fma_f2(f2(sv[base + 2 * i], sv[base + 2 * i + 1]), sl2x2, nmx2), x0, x1);
+    a = ex2(x0);
+    c = ex2(x1);
+    ls = add_f2(ls, f2(a, c));
+    pk = pack2_int<BF16>(a, c);
+  };
+  // P for keys 0-63 goes to TMEM first so that the P*V MMA can start on
+  // that half while the exponentials of keys 64-127 are computed.
+#pragma unroll
+  for (int i = 0; i < 32; ++i) exp_pair(0, i, pk0[i], (i & 1) ? ls1 : ls0);
+  if (resc != 0.f) {
+    // O of the previous blocks is complete: s_full of this block was
+    // committed after their P*V MMAs.  P*V of this block waits for p_ready.
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32(tO + c * 32, o);
+      wait_ld_dep(o);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * resc);
+      tmem_st32(tO + c * 32, o);
+    }
+  }
+  tmem_st32(tS + 0, pk0);
+  tmem_wait_st();
+  tc_fence_before();
+  release(0);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) exp_pair(64, i, pk1[i], (i & 1) ? ls1 : ls0);
+  {
+    float a0, a1, b0, b1;
+    f2_split(ls0, a0, a1);
+    f2_split(ls1, b0, b1);
+    l += (a0 + b0) + (a1 + b1);
+  }
+  tmem_st32(tS + 32, pk1);
+  tmem_wait_st();
+  tc_fence_before();
+  release(1);
+}
+
 template <int D, bool BF16>
 __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_constant__ FwdParams p) {
   using C = FwdCfg<D>;
@@ -275,97 +376,8 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
     for (int j = 0; j < nb[w]; ++j) {
       if (!(ok = mbar_wait(&s_full[w], j & 1, abort_flag))) break;
       tc_fence_after();
-      uint32_t r0[32], r1[32], r2[32], r3[32];
-      tmem_ld32(tS + 0, r0);
-      tmem_ld32(tS + 32, r1);
-      tmem_ld32(tS + 64, r2);
-      tmem_ld32(tS + 96, r3);
-      wait_ld_dep(r0);
-      wait_ld_dep(r1);
-      wait_ld_dep(r2);
-      wait_ld_dep(r3);
-      float sv[128];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        sv[i] = __uint_as_float(r0[i]);
-        sv[32 + i] = __uint_as_float(r1[i]);
-        sv[64 + i] = __uint_as_float(r2[i]);
-        sv[96 + i] = __uint_as_float(r3[i]);
-      }
-      const int kbase = j * 128;
-      if ((p.causal && kbase + 127 > qt * 128) || kbase + 128 > p.S) {
-        const int lim = min(p.S - kbase, p.causal ? qrow - kbase + 1 : 128);
-#pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (c >= lim) sv[c] = -INFINITY;
-      }
-      float mx0 = sv[0], mx1 = sv[1], mx2 = sv[2], mx3 = sv[3];
-#pragma unroll
-      for (int c = 4; c < 128; c += 8) {
-        mx0 = fmax3(mx0, sv[c], sv[c + 1]);
-        mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
-        mx2 = fmax3(mx2, sv[c + 4], sv[c + 5]);
-        mx3 = fmax3(mx3, sv[c + 6], sv[c + 7]);
-      }
-      const float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
-      // Raise the running max when this block's exceeds it by more than 8
-      // (2^8 headroom in fp32): the row sum now, the partial O row below,
-      // after the first half's exponentials, when half of S is no longer
-      // live in registers (the O chunks then fit without spilling).
-      float resc = 0.f;
-      if (j == 0) {
-        m_used = (mx == -INFINITY) ? 0.f : mx;
-      } else if (mx > m_used + 8.0f) {
-        resc = ex2(m_used - mx);
-        l *= resc;
-        m_used = mx;
-      }
-      const uint64_t sl2x2 = f2(sl2, sl2), nmx2 = f2(-m_used, -m_used);
-      uint32_t pk0[32], pk1[32];
-      uint64_t ls0 = f2(0.f, 0.f), ls1 = f2(0.f, 0.f);
-      // exponentials of keys 2i, 2i+1 (pair i of the half at sv + base): the
-      // scale and the row sums in packed f32x2 instructions
-      auto exp_pair = [&](int base, int i, uint32_t& pk, uint64_t& ls) {
-        float x0, x1, a, c;
-        f2_split(fma_f2(f2(sv[base + 2 * i], sv[base + 2 * i + 1]), sl2x2, nmx2), x0, x1);
-        a = ex2(x0);
-        c = ex2(x1);
-        ls = add_f2(ls, f2(a, c));
-        pk = pack2_int<BF16>(a, c);
-      };
-      // P for keys 0-63 goes to TMEM first so that the P*V MMA can start on
-      // that half while the exponentials of keys 64-127 are computed.
-#pragma unroll
-      for (int i = 0; i < 32; ++i) exp_pair(0, i, pk0[i], (i & 1) ? ls1 : ls0);
-      if (resc != 0.f) {
-        // O of the previous blocks is complete: s_full of this block was
-        // committed after their P*V MMAs.  P*V of this block waits for p_ready.
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          wait_ld_dep(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * resc);
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      tmem_st32(tS + 0, pk0);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_ready[2 * w]);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) exp_pair(64, i, pk1[i], (i & 1) ? ls1 : ls0);
-      {
-        float a0, a1, b0, b1;
-        f2_split(ls0, a0, a1);
-        f2_split(ls1, b0, b1);
-        l += (a0 + b0) + (a1 + b1);
-      }
-      tmem_st32(tS + 32, pk1);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_ready[2 * w + 1]);
+      softmax_block<D, BF16>(tS, tO, sl2, j, qt, qrow, p.S, p.causal, m_used, l,
+                             [&](int hh) { mbar_arrive(&p_ready[2 * w + hh]); });
     }
     if (ok && nb[w] > 0 && mbar_wait(&o_done[w], 0, abort_flag)) {
       tc_fence_after();

@@ -190,6 +190,18 @@ static int bwd_needs_input(const TkmGraph *g, const PlasmaGroup *pg) {
 
 int tkm_group_bwd_row_inputs(const TkmGraph *g, const PlasmaGroup *pg) { return bwd_staged_rows(g, pg); }
 
+/* Row blocks in flight in a staged kernel's cp.async ring (its slots):
+ * TKM_FWD_SLOTS / TKM_BWD_SLOTS (2-4) override the default of 2.  Measured
+ * at configuration 3 (same box, alternated twice): 3 or 4 backward slots
+ * left the norm backward at 145-150 us (2: 145 us) and slowed the twin
+ * backward (338 -> 350-369 us); 3 forward slots slowed the norm forward
+ * (66 -> 68-69 us).  The rows are not latency-bound at two slots. */
+static int stage_slots(int bwd) {
+    const char *e = getenv(bwd ? "TKM_BWD_SLOTS" : "TKM_FWD_SLOTS");
+    const int v = e ? atoi(e) : 2;
+    return v < 2 ? 2 : (v > 4 ? 4 : v);
+}
+
 /* Forward row staging: the row inputs (the group input, both halves for a
  * twin, and every Add branch) of the next two row blocks are brought by
  * cp.async into dynamic shared memory while the current one computes.
@@ -206,7 +218,7 @@ static int fwd_stage_bytes_raw(const TkmGraph *g, const PlasmaGroup *pg, int act
     for (int i = 0; i < L.n; i++)
         if (g->nodes[L.ids[i]].op == OP_ADD) n++;
     if (gm.persist && n < 2) return 0;
-    const long bytes = 2L * n * gm.kch * gm.threads * 16;
+    const long bytes = (long)stage_slots(0) * n * gm.kch * gm.threads * 16;
     return bytes <= 128 * 1024 ? (int)bytes : 0;
 }
 
@@ -229,7 +241,7 @@ int tkm_group_bwd_stage_bytes(const TkmGraph *g, const PlasmaGroup *pg, int act_
     if (nrows < 2) return 0;
     TkmRowGeom gm;
     tkm_row_geom_bwd(g, pg, act_bytes, &gm);
-    const long bytes = 2L * nrows * gm.kch * gm.threads * 16;
+    const long bytes = (long)stage_slots(1) * nrows * gm.kch * gm.threads * 16;
     return bytes <= 128 * 1024 ? (int)bytes : 0;
 }
 
@@ -816,14 +828,15 @@ static void emit_geom_macros(Em *e, int bwd) {
                 bwd ? tkm_group_bwd_stage_bytes(e->g, e->pg, i == 0 ? 2 : 4)
                     : tkm_group_fwd_stage_bytes(e->g, e->pg, i == 0 ? 2 : 4));
     }
-    bprintf(b, "#endif\n#define TKG_C2 %d\n#define TKG_ROWS %d\n#define TKG_INV_C ", g2.C2, g2.rows);
+    bprintf(b, "#endif\n#define TKG_NSLOT %d\n#define TKG_C2 %d\n#define TKG_ROWS %d\n#define TKG_INV_C ",
+            stage_slots(bwd), g2.C2, g2.rows);
     emit_float(b, 1.0 / (double)g2.C);
     bprintf(b, "\n#define TKG_NRB ((TKG_ROWS + TKG_RPB - 1) / TKG_RPB)\n");
 }
 
 static void undef_geom(Buf *b) {
     bprintf(b, "#undef TKG_VP\n#undef TKG_NCH\n#undef TKG_TPR\n#undef TKG_KCH\n#undef TKG_RPB\n#undef TKG_THREADS\n#undef TKG_CB\n"
-               "#undef TKG_STAGE_BYTES\n"
+               "#undef TKG_STAGE_BYTES\n#undef TKG_NSLOT\n"
                "#undef TKG_C2\n#undef TKG_ROWS\n#undef TKG_INV_C\n#undef TKG_NRB\n");
 }
 
@@ -993,7 +1006,7 @@ static void emit_fwd_body(Em *e) {
 }
 
 /* Staged forward (tkm_group_fwd_stage_bytes).  TKG_STAGE_BYTES > 0:
- * persistent, the row inputs of the next two row blocks staged by cp.async in
+ * persistent, the row inputs of the next TKG_NSLOT row blocks staged by cp.async in
  * dynamic shared memory; else (a normalisation group whose stages would not
  * fit) one row block per block. */
 static void emit_plasma_fwd_rowblock(Em *e) {
@@ -1011,7 +1024,7 @@ static void emit_plasma_fwd_rowblock(Em *e) {
                "  extern __shared__ uint4 tkm_dyn[];\n"
                "#define TKM_STG(s, a, k) tkm_dyn[(((s) * %d + (a)) * TKG_KCH + (k)) * TKG_THREADS + threadIdx.x]\n",
             nin);
-    for (int ahead = 0; ahead < 2; ahead++) {
+    for (int ahead = 0; ahead < stage_slots(0); ahead++) {
         bprintf(b, "  {\n    const int rbn = blockIdx.x + %d * gridDim.x;\n", ahead);
         emit_stage_issue(e, in, nin, "%d", ahead);
         bprintf(b, "  }\n  tkm_cp_commit();\n");
@@ -1020,14 +1033,14 @@ static void emit_plasma_fwd_rowblock(Em *e) {
                "  for (int tkm_rb = blockIdx.x; tkm_rb < TKG_NRB; tkm_rb += gridDim.x, ++tkm_it) {\n"
                "  const int row = tkm_rb * TKG_RPB + threadIdx.x / TKG_TPR;\n"
                "  const bool tkm_row_ok = row < TKG_ROWS;\n"
-               "  const int tkm_sl = tkm_it & 1;\n  tkm_cp_wait<1>();\n");
+               "  const int tkm_sl = tkm_it %% TKG_NSLOT;\n  tkm_cp_wait<TKG_NSLOT - 1>();\n");
     declare_stats(e);
     for (int i = 0; i < nin; i++) {
         decl_array(b, in[i].arr);
         bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) tkm_lds<TKG_VP>(&TKM_STG(tkm_sl, %d, k), %s[k]);\n",
                 i, in[i].arr);
     }
-    bprintf(b, "  {\n    const int rbn = tkm_rb + 2 * gridDim.x;\n");
+    bprintf(b, "  {\n    const int rbn = tkm_rb + TKG_NSLOT * gridDim.x;\n");
     emit_stage_issue(e, in, nin, "tkm_sl", -1);
     bprintf(b, "  }\n  tkm_cp_commit();\n");
     emit_fwd_body(e);
@@ -1212,14 +1225,14 @@ static void emit_plasma_bwd(Em *e) {
         rin[nin++] = f;
     }
     /* TKG_STAGE_BYTES > 0 (per storage type, tkm_group_bwd_stage_bytes):
-     * rows are staged two row blocks ahead by cp.async into dynamic
+     * rows are staged TKG_NSLOT row blocks ahead by cp.async into dynamic
      * shared-memory slots private to each thread, so that their loads are in
      * flight while the current row computes, without holding registers. */
     bprintf(b, "#if TKG_STAGE_BYTES > 0\n"
                "  extern __shared__ uint4 tkm_dyn[];\n"
                "#define TKM_STG(s, a, k) tkm_dyn[(((s) * %d + (a)) * TKG_KCH + (k)) * TKG_THREADS + threadIdx.x]\n",
             nin);
-    for (int ahead = 0; ahead < 2; ahead++) {
+    for (int ahead = 0; ahead < stage_slots(1); ahead++) {
         bprintf(b, "  {\n    const int rbn = blockIdx.x + %d * gridDim.x;\n", ahead);
         emit_stage_issue(e, rin, nin, "%d", ahead);
         bprintf(b, "  }\n  tkm_cp_commit();\n");
@@ -1234,13 +1247,13 @@ static void emit_plasma_bwd(Em *e) {
         bprintf(b, "  float2 tdbr[TKG_KCH][TKG_VP];\n"
                    "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) _Pragma(\"unroll\") for (int q = 0; q < TKG_VP; ++q)\n"
                    "    tdbr[k][q] = make_float2(0.f, 0.f);\n");
-    bprintf(b, "#if TKG_STAGE_BYTES > 0\n  const int tkm_sl = tkm_it & 1;\n  tkm_cp_wait<1>();\n");
+    bprintf(b, "#if TKG_STAGE_BYTES > 0\n  const int tkm_sl = tkm_it %% TKG_NSLOT;\n  tkm_cp_wait<TKG_NSLOT - 1>();\n");
     for (int i = 0; i < nin; i++) {
         decl_array(b, rin[i].arr);
         bprintf(b, "  _Pragma(\"unroll\") for (int k = 0; k < TKG_KCH; ++k) tkm_lds<TKG_VP>(&TKM_STG(tkm_sl, %d, k), %s[k]);\n",
                 i, rin[i].arr);
     }
-    bprintf(b, "  {\n    const int rbn = tkm_rb + 2 * gridDim.x;\n");
+    bprintf(b, "  {\n    const int rbn = tkm_rb + TKG_NSLOT * gridDim.x;\n");
     emit_stage_issue(e, rin, nin, "tkm_sl", -1);
     bprintf(b, "  }\n  tkm_cp_commit();\n#else\n");
     for (int i = 0; i < nin; i++) load_array(b, rin[i].arr, rin[i].src, rin[i].stride, rin[i].col0);
