@@ -86,10 +86,9 @@ TKB_DEVFN void fwd_cta_order(int cta, int BH, int npairs, int hg, int& bh, int& 
 }
 
 // One key block of the online softmax for this thread's query row: S from
-// TMEM, the causal and
-// sequence-end masks, the running max raised when this block's exceeds it
-// by more than 8 (rescaling O in TMEM), P written over S in two halves, and
-// release(h) once half h (keys 64h .. 64h+63) is in TMEM.
+// TMEM, the causal and sequence-end masks, the running max raised when this
+// block's exceeds it by more than 8 (rescaling O in TMEM), P written over S
+// in two halves, and release(h) once half h (keys 64h .. 64h+63) is in TMEM.
 template <int D, bool BF16, typename Release>
 TKB_DEVFN void softmax_block(uint32_t tS, uint32_t tO, float sl2, int j, int qt, int qrow, int S, int causal,
                              float& m_used, float& l, Release&& release) {
