@@ -109,8 +109,8 @@ struct DkvCfg {
   static constexpr int OFF_LSE = OFF_DO + NSTQ * TILE;  // NSTQ x 128 floats
   static constexpr int OFF_DEL = OFF_LSE + NSTQ * 512;
   static constexpr int OFF_BAR = OFF_DEL + NSTQ * 512;
-  // kv_full, q_full[NSTQ], q_empty[NSTQ], st_full[2], dp_full, p_ready, ds_ready, kv_done, drain
-  static constexpr int NBAR = 1 + 2 * NSTQ + 7;
+  // kv_full, q_full[NSTQ], q_empty[NSTQ], st_full[2], dp_full, p_ready[2], ds_ready, kv_done, drain
+  static constexpr int NBAR = 1 + 2 * NSTQ + 8;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int SMEM = OFF_MISC + 16 + 1024;
   static constexpr uint32_t TM_DP = 128, TM_DK = 256, TM_DV = 256 + D;
@@ -130,8 +130,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
   uint64_t* q_empty = q_full + C::NSTQ;
   uint64_t* st_full = q_empty + C::NSTQ;  // [S^T buffer]
   uint64_t* dp_full = st_full + 2;
-  uint64_t* p_ready = dp_full + 1;
-  uint64_t* ds_ready = p_ready + 1;
+  uint64_t* p_ready = dp_full + 1;  // [half]: P^T of queries 0-31 / 32-63 of each compute warpgroup
+  uint64_t* ds_ready = p_ready + 2;
   uint64_t* kv_done = ds_ready + 1;
   uint64_t* mma_drain = kv_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
@@ -157,7 +157,8 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
     mbar_init(&st_full[0], 1);
     mbar_init(&st_full[1], 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_ready, 256);
+    mbar_init(&p_ready[0], 256);
+    mbar_init(&p_ready[1], 256);
     mbar_init(ds_ready, 256);
     mbar_init(kv_done, 1);
     mbar_init(mma_drain, 1);
@@ -234,6 +235,16 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
           umma_ts(d, a_tm + half_split_col(kk), sdesc_sw128(bm + kk * 2048, C::SLAB, 1024), idKV,
                   (acc || kk > 0) ? 1u : 0u);
       };
+      // the same over the K-steps of one half of each warpgroup's queries:
+      // half 0 = K-steps 0, 1 (group 0) and 4, 5 (group 1), half 1 = the rest
+      auto issue_acc_half = [&](uint32_t d, uint32_t a_tm, uint32_t bm, bool acc, int half) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int kk = (i >> 1) * 4 + half * 2 + (i & 1);
+          umma_ts(d, a_tm + half_split_col(kk), sdesc_sw128(bm + kk * 2048, C::SLAB, 1024), idKV,
+                  (acc || i > 0) ? 1u : 0u);
+        }
+      };
       // S^T of step n into its buffer; st_full[buffer] completes once per use
       auto issue_st = [&](int n) {
         issue_nt(tmem + C::tm_st(n), sK, sQ(n % C::NSTQ));
@@ -255,9 +266,13 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
       for (int it = 0; ok && it < n_steps; ++it) {
         const int s = it % C::NSTQ, s1 = (it + 1) % C::NSTQ;
         const bool more = it + 1 < n_steps;
-        if (!(ok = mbar_wait(p_ready, it & 1, abort_flag))) break;
+        // dV += P^T dO, in two halves as the compute warps publish P^T
+        if (!(ok = mbar_wait(&p_ready[0], it & 1, abort_flag))) break;
         tc_fence_after();
-        issue_acc(tmem + C::TM_DV, tmem + C::tm_st(it), sO(s), it > 0);       // dV += P^T dO
+        issue_acc_half(tmem + C::TM_DV, tmem + C::tm_st(it), sO(s), it > 0, 0);
+        if (!(ok = mbar_wait(&p_ready[1], it & 1, abort_flag))) break;
+        tc_fence_after();
+        issue_acc_half(tmem + C::TM_DV, tmem + C::tm_st(it), sO(s), true, 1);
         // the S^T MMA that reuses this buffer (step it + 2 with two buffers,
         // it + 1 with one) follows the dV MMA that reads P^T from it
         const int nxt = C::DBL ? it + 2 : it + 1;
@@ -315,8 +330,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
         // masked keys (sequence tail) and the diagonal tile need the per-element test
         const bool need_mask = !key_ok || qmin > 0;
         const uint64_t sl2x2 = f2(sl2, sl2);
-#pragma unroll
-        for (int e4 = 0; e4 < 16; ++e4) {
+        // P^T of queries 0-31 of this warpgroup first (K-steps released to the
+        // dV MMA while queries 32-63 are computed), then the rest
+        auto exp4 = [&](int e4) {
           const float4 l = lse4[e4];  // -LSE * log2(e) of queries 4 e4 .. 4 e4 + 3
           const uint32_t* src = e4 < 8 ? &v0[e4 * 4] : &v1[(e4 - 8) * 4];
           const int q0 = e4 * 4;
@@ -340,12 +356,20 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
           }
           pk[e4 * 2] = pack2<BF16>(a0, a1);
           pk[e4 * 2 + 1] = pack2<BF16>(a2, a3);
-        }
+        };
+#pragma unroll
+        for (int e4 = 0; e4 < 8; ++e4) exp4(e4);
+        tmem_st16(tST, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[0]);
+#pragma unroll
+        for (int e4 = 8; e4 < 16; ++e4) exp4(e4);
+        tmem_st16(tST + 16, pk + 16);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_ready[1]);
       }
-      tmem_st32(tST, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(p_ready);
 
       if (!(ok = mbar_wait(dp_full, it & 1, abort_flag))) break;
       tc_fence_after();
