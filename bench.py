@@ -542,8 +542,10 @@ def measure_train(args, world, rank, local, dev, cfg, steps, warmup):
                      "overlap": "issued on a second stream as the backward completes each bucket; "
                                 "the SGD update waits for the last"}
 
-    # end to end: pinned host embeddings + labels uploaded every step, loss read back
-    e2e_steps = 4
+    # end to end: pinned host embeddings + labels uploaded every step, loss read
+    # back; as many steps as the resident loop, so that one slow host call
+    # (seen up to 150 ms against 88) weighs as little as in the resident rate
+    e2e_steps = max(4, steps)
     host_ms = []
     dist_barrier(world)
     t0 = torch.cuda.Event(enable_timing=True)
