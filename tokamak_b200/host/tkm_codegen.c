@@ -109,7 +109,13 @@ void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRo
         if ((nch + o->kch - 1) / o->kch > 1024) o->kch = (nch + 1023) / 1024;
         o->tpr = round_up((nch + o->kch - 1) / o->kch, 32);
     } else {
-        o->ncb = (nch + 255) / 256;
+        /* column blocks of at most 256 threads; a twin epilogue's of up to
+         * 1024 (configuration 3, same box, alternated twice: twin forward
+         * 184-186 -> 166 us, backward 360-370 -> 335-337 us with 1024;
+         * the one-input Bias on 32000-wide rows is best at 256: 176 us
+         * there, 204 us at 1024) */
+        const int cap = pg->is_twin_epilogue ? 1024 : 256;
+        o->ncb = (nch + cap - 1) / cap;
         o->tpr = round_up((nch + o->ncb - 1) / o->ncb, 32);
     }
     o->rpb = o->tpr >= 256 ? 1 : 256 / o->tpr;
