@@ -157,7 +157,8 @@ size_t tkb_softmax_loss_workspace(int rows);
  * int32 per row (the reference reads uint8 labels[r], src/tkm_gpu.cu:646).
  * loss += mean over rows (summed in a fixed order); dlogits = dloss/dlogits
  * (may be NULL); correct += number of rows whose argmax equals the label
- * (may be NULL).  C <= 32768. */
+ * (may be NULL).  C <= 32768.  logits and dlogits 16-byte aligned when
+ * C % 8 == 0 (else aligned to two elements); TKB_ERR_ARG otherwise. */
 int tkb_softmax_loss(const void *logits, const int32_t *labels, void *dlogits,
                      float *loss, int *correct, void *workspace, size_t workspace_bytes,
                      int rows, int C, int kind, float gamma, int dtype, void *stream);
@@ -170,7 +171,8 @@ int tkb_softmax_loss(const void *logits, const int32_t *labels, void *dlogits,
  * the library (1 MiB per GPU, held until exit), so rows must be at most
  * 262144; larger calls return TKB_ERR_ARG.  The first call on a device looks up
  * the array's address for that device: make it before any stream capture.
- * All calls share the array; calls that overlap on the GPU race on it. */
+ * All calls share the array; calls that overlap on the GPU race on it.
+ * Alignment as for tkb_softmax_loss. */
 int tkb_softmax_loss_noalloc(const void *logits, const int32_t *labels, void *dlogits,
                              float *loss, int *correct, int rows, int C, int kind, float gamma,
                              int dtype, void *stream);

@@ -51,6 +51,16 @@ def test_argument_errors_without_device():
     # missing workspace
     rc = L.tkb_softmax_loss(vp(16), None, None, vp(16), None, None, 0, 4, 8, 0, 2.0, 1, None)
     assert rc == -4
+    # rows of a multiple of 8 move in 16-byte vectors (bulk copies at 8192-32768):
+    # an 8-byte-aligned pointer is refused, as is a 2-byte one for odd pairs
+    rc = L.tkb_softmax_loss(vp(24), None, None, None, None, None, 0, 4, 32000, 0, 2.0, 1, None)
+    assert rc == -1 and b"16-byte aligned" in L.tkb_last_error()
+    rc = L.tkb_softmax_loss(vp(16), None, vp(40), None, None, None, 0, 4, 32000, 0, 2.0, 1, None)
+    assert rc == -1
+    rc = L.tkb_softmax_loss(vp(18), None, None, None, None, None, 0, 4, 10, 0, 2.0, 1, None)
+    assert rc == -1
+    rc = L.tkb_softmax_loss_noalloc(vp(24), None, None, None, None, 4, 32000, 0, 2.0, 1, None)
+    assert rc == -1 and b"16-byte aligned" in L.tkb_last_error()
 
 
 def test_workspace_sizes():

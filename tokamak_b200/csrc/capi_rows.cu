@@ -12,6 +12,15 @@ int row_check(const char* who, int rows, int C, int dtype) {
   return TKB_OK;
 }
 
+// Row pointers for the softmax losses: rows whose width is a multiple of 8
+// move in 16-byte vectors (and 16-bit rows of 8192-32768 by bulk copies,
+// which need 16-byte addresses); other widths in pairs of elements.
+bool loss_rows_aligned(const void* p, int C, int dtype) {
+  if (!p) return true;
+  const uintptr_t need = C % 8 == 0 ? 16u : (dtype == TKB_F32 ? 8u : 4u);
+  return reinterpret_cast<uintptr_t>(p) % need == 0;
+}
+
 // Calls F<T>(...) for the runtime dtype.
 #define TKB_BY_DTYPE(DT, CALL)                         \
   ((DT) == TKB_F32    ? CALL(float)                    \
@@ -194,6 +203,9 @@ int tkb_softmax_loss(const void* logits, const int32_t* labels, void* dlogits, f
   if (!logits) return fail(TKB_ERR_ARG, "tkb_softmax_loss: null logits");
   if (kind < 0 || kind > 2) return fail(TKB_ERR_ARG, "tkb_softmax_loss: kind %d not in {0,1,2}", kind);
   if (C > 256 * 8 * 16) return fail(TKB_ERR_UNSUPPORTED, "tkb_softmax_loss: C > 32768");
+  if (!loss_rows_aligned(logits, C, dtype) || !loss_rows_aligned(dlogits, C, dtype))
+    return fail(TKB_ERR_ARG, "tkb_softmax_loss: logits and dlogits must be 16-byte aligned when C %% 8 == 0 "
+                "(else aligned to two elements)");
   if (loss && (!workspace || workspace_bytes < tkb_softmax_loss_workspace(rows)))
     return fail(TKB_ERR_WORKSPACE, "tkb_softmax_loss: workspace of %zu bytes required", tkb_softmax_loss_workspace(rows));
   cudaStream_t st = static_cast<cudaStream_t>(stream);

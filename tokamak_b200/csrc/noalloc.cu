@@ -77,6 +77,9 @@ extern "C" int tkb_softmax_loss_noalloc(const void* logits, const int32_t* label
   if (!logits) return fail(TKB_ERR_ARG, "tkb_softmax_loss_noalloc: null logits");
   if (kind < 0 || kind > 2) return fail(TKB_ERR_ARG, "tkb_softmax_loss_noalloc: kind %d not in {0,1,2}", kind);
   if (C > 256 * 8 * 16) return fail(TKB_ERR_UNSUPPORTED, "tkb_softmax_loss_noalloc: C > 32768");
+  if (!loss_rows_aligned(logits, C, dtype) || !loss_rows_aligned(dlogits, C, dtype))
+    return fail(TKB_ERR_ARG, "tkb_softmax_loss_noalloc: logits and dlogits must be 16-byte aligned when C %% 8 == 0 "
+                "(else aligned to two elements)");
   if (rows > kNoallocMaxRows)
     return fail(TKB_ERR_ARG, "tkb_softmax_loss_noalloc: rows %d exceeds the built-in scratch limit of %d rows", rows,
                 kNoallocMaxRows);

@@ -15,8 +15,10 @@
 // Pairs (of the four in each 16-byte vector) whose exponentials the
 // bulk-staged softmax loss computes with the FMA-pipe polynomial
 // (ex2_poly_f2, relative error 1.02e-4) instead of ex2, to offload the MUFU
-// unit the kernel keeps busy: same box, 8192 x 32000 bf16, 0.2222 ms with
-// none, 0.2181 with one, 0.2245 with two.
+// unit the kernel keeps busy.  Same box, 8192 x 32000 bf16: 0.2222 ms with
+// none, 0.2181 with one, 0.2245 with two in the register form that preceded
+// the bulk-staged kernel; 189.4 us with one and 189.5 with two in the
+// bulk-staged kernel.
 #ifndef TKB_CE_EMU
 #define TKB_CE_EMU 1
 #endif
@@ -720,6 +722,7 @@ __global__ void __launch_bounds__(NTH) softmax_loss_kernel(const T* __restrict__
 // argmax, the label logit); pass 2 reads the row again and writes the
 // gradient, re-reading global memory (mostly L2) with eight rows in flight
 // per SM.  Used for rows wider than 72 KB; narrower wide rows take
+// softmax_loss_bulk_kernel (16-bit, 8192-32768 wide) or
 // softmax_loss_staged_kernel.  Same results as softmax_loss_kernel
 // (src/tkm_gpu.cu:632-682).
 template <typename T, int VEC>
