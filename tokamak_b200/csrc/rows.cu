@@ -1338,6 +1338,10 @@ __global__ void __launch_bounds__(512, 1) softmax_loss_bulk_kernel(const T* __re
     mbar_arrive_expect_tx(bar, row_bytes);
     bulk_load(smem_raw + (j % ns) * pitch, logits + static_cast<long long>(r) * C, row_bytes, bar);
   };
+  if (ns < 1 || ns > 8 || pitch < static_cast<int>(row_bytes) || (pitch & 15)) {  // launch contract of the host side
+    if (threadIdx.x == 0) atomicOr(&g_device_error, ERR_BAD_LAUNCH);
+    return;
+  }
   if (threadIdx.x == 0) {
     for (int j = 0; j < ns; ++j) mbar_init(&full[j], 1);
     abort_flag = 0;
