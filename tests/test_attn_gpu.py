@@ -71,6 +71,31 @@ def test_attn_fwd_bwd_16bit(rng, B, S, Hq, Hkv, D, causal, dtype, keep_ds):
         assert err < TOL16, (name, err)
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+def test_attn_fwd_running_max_jumps(rng, D, causal):
+    """The forward's lazy rescale: odd query rows scaled by 150, so their
+    scores spread over hundreds of log2 units and their running maximum
+    jumps past the rescale threshold at different key blocks, while the
+    even rows of the same warp rarely do (12 to 16 of the 16 warps mixed);
+    30-70 rows jump by more than 126, where the rescale factor is 0 and the
+    partial O of the earlier blocks must be cleared, not kept."""
+    ops = _ops()
+    B, S, Hq, Hkv = 1, 512, 2, 1
+    qkv = rng.standard_normal((B, S, (Hq + 2 * Hkv) * D)).astype(np.float32)
+    qkv[0, 1::2, :Hq * D] *= 150.0
+    tq = torch.from_numpy(qkv).to("cuda", torch.bfloat16)
+    qkv = tq.float().cpu().numpy()
+    scale = D ** -0.5
+    ref_o, ref_lse = oracle.attn_fwd(qkv, B, S, Hq, Hkv, D, scale, causal)
+    o, lse = ops.gqa_attn_fwd(tq, B, S, Hq, Hkv, D, scale, causal)
+    torch.cuda.synchronize()
+    o_np = o.float().cpu().numpy()
+    assert np.isfinite(o_np).all()
+    assert rel_l2(o_np, ref_o) < TOL16, rel_l2(o_np, ref_o)
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() < 2e-2 * max(1.0, np.abs(ref_lse).max() / 100)
+
+
 @pytest.mark.parametrize("B,S,Hq,Hkv,D,causal", [(1, 128, 2, 1, 64, True), (2, 96, 4, 2, 128, False),
                                                    (1, 130, 2, 2, 64, True)])
 def test_attn_fp32_mode(rng, B, S, Hq, Hkv, D, causal):

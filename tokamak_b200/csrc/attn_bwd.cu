@@ -317,8 +317,9 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
       // keys above the diagonal of a diagonal tile see no query of this half below qmin
       const int qmin = (p.causal && i == jt) ? kr - w * 64 : -1;
       const uint32_t tST = tmem + lane_off + C::tm_st(it) + cb;
-      if (!(ok = mbar_wait(&q_full[s], (it / C::NSTQ) & 1, abort_flag))) break;
-      if (!(ok = mbar_wait(&st_full[C::DBL ? (it & 1) : 0], C::DBL ? ((it >> 1) & 1) : (it & 1), abort_flag))) break;
+      if (!(ok = mbar_wait_warp(&q_full[s], (it / C::NSTQ) & 1, abort_flag))) break;
+      if (!(ok = mbar_wait_warp(&st_full[C::DBL ? (it & 1) : 0], C::DBL ? ((it >> 1) & 1) : (it & 1), abort_flag)))
+        break;
       tc_fence_after();
       uint32_t pk[32];
       {
@@ -371,7 +372,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
         mbar_arrive(&p_ready[1]);
       }
 
-      if (!(ok = mbar_wait(dp_full, it & 1, abort_flag))) break;
+      if (!(ok = mbar_wait_warp(dp_full, it & 1, abort_flag))) break;
       tc_fence_after();
       uint32_t ds[32];
       {
@@ -412,7 +413,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dkdv_kernel(const __grid_cons
       }
     }
     // epilogue: warpgroup 0 stores dK (scaled), warpgroup 1 stores dV
-    if (ok && mbar_wait(kv_done, 0, abort_flag)) {
+    if (ok && mbar_wait_warp(kv_done, 0, abort_flag)) {
       tc_fence_after();
       const float mul = w == 0 ? p.scale : 1.0f;
       uint8_t* dst = reinterpret_cast<uint8_t*>(w == 0 ? p.dk : p.dv) +
@@ -639,7 +640,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
       const int kbase = j * 128 + w * 64;
       // keys >= lim are masked (sequence end, causal diagonal)
       const int lim = min(p.S - kbase, p.causal ? qrow - kbase + 1 : 64);
-      if (!(ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag))) break;
+      if (!(ok = mbar_wait_warp(&s_full[j & 1], (j >> 1) & 1, abort_flag))) break;
       tc_fence_after();
       float pv[64];
       {
@@ -661,7 +662,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
             if (c >= lim) pv[c] = 0.f;
         }
       }
-      if (!(ok = mbar_wait(dp_full, j & 1, abort_flag))) break;
+      if (!(ok = mbar_wait_warp(dp_full, j & 1, abort_flag))) break;
       tc_fence_after();
       uint32_t ds[32];
       {
@@ -684,7 +685,7 @@ __global__ void __launch_bounds__(320, 1) attn_bwd_dq_kernel(const __grid_consta
       mbar_arrive(ds_ready);
     }
     // epilogue: each warpgroup stores half of the D columns of dQ (scaled)
-    if (ok && mbar_wait(dq_done, 0, abort_flag)) {
+    if (ok && mbar_wait_warp(dq_done, 0, abort_flag)) {
       tc_fence_after();
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.dq) +
                      2 * (static_cast<long long>(b) * p.dkv_batch_stride +
@@ -884,7 +885,7 @@ __global__ void __launch_bounds__(192, 1) attn_bwd_dsk_kernel(const __grid_const
     for (int t = blockIdx.x; t < n_items; t += gridDim.x, ++k) {
       const DskItem it = dsk_item<D>(p, t);
       const int a = k & 1;
-      if (!mbar_wait(&acc_full[a], (k >> 1) & 1, abort_flag)) break;
+      if (!mbar_wait_warp(&acc_full[a], (k >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       const int b = it.bh / p.Hq, h = it.bh % p.Hq;
       const int qrow = it.qt * 128 + r;

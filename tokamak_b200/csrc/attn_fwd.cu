@@ -129,13 +129,15 @@ TKB_DEVFN void softmax_block(uint32_t tS, uint32_t tO, float sl2, int j, int qt,
   // (2^8 headroom in fp32): the row sum now, the partial O row below,
   // after the first half's exponentials, when half of S is no longer
   // live in registers (the O chunks then fit without spilling).
-  float resc = 0.f;
+  float resc = 1.f;
+  bool raised = false;
   if (j == 0) {
     m_used = (mx == -INFINITY) ? 0.f : mx;
   } else if (mx > m_used + 8.0f) {
-    resc = ex2(m_used - mx);
+    resc = ex2(m_used - mx);  // may be 0 for a jump past 2^126: O is then cleared
     l *= resc;
     m_used = mx;
+    raised = true;
   }
   const uint64_t sl2x2 = f2(sl2, sl2), nmx2 = f2(-m_used, -m_used);
   uint32_t pk0[32], pk1[32];
@@ -154,9 +156,12 @@ TKB_DEVFN void softmax_block(uint32_t tS, uint32_t tO, float sl2, int j, int qt,
   // that half while the exponentials of keys 64-127 are computed.
 #pragma unroll
   for (int i = 0; i < 32; ++i) exp_pair(0, i, pk0[i], (i & 1) ? ls1 : ls0);
-  if (resc != 0.f) {
-    // O of the previous blocks is complete: s_full of this block was
-    // committed after their P*V MMAs.  P*V of this block waits for p_ready.
+  if (__any_sync(0xffffffffu, raised)) {
+    // The warp rescales its 32 rows of O if any of them raised its maximum
+    // (rows that did not multiply by 1): tcgen05.ld / st are warp-collective
+    // and must not run under a per-row condition.  O of the previous blocks
+    // is complete: s_full of this block was committed after their P*V MMAs.
+    // P*V of this block waits for p_ready.
 #pragma unroll 1
     for (int c = 0; c < D / 32; ++c) {
       uint32_t o[32];
@@ -373,12 +378,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_tc_kernel(const __grid_consta
     float m_used = 0.f, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nb[w]; ++j) {
-      if (!(ok = mbar_wait(&s_full[w], j & 1, abort_flag))) break;
+      if (!(ok = mbar_wait_warp(&s_full[w], j & 1, abort_flag))) break;
       tc_fence_after();
       softmax_block<D, BF16>(tS, tO, sl2, j, qt, qrow, p.S, p.causal, m_used, l,
                              [&](int hh) { mbar_arrive(&p_ready[2 * w + hh]); });
     }
-    if (ok && nb[w] > 0 && mbar_wait(&o_done[w], 0, abort_flag)) {
+    if (ok && nb[w] > 0 && mbar_wait_warp(&o_done[w], 0, abort_flag)) {
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.0f / l : 0.f;
       const bool valid = qrow < p.S;

@@ -89,6 +89,14 @@ TKB_DEVFN bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_fla
   }
 }
 
+// The same for a whole warp, with one result for every lane: a wait that
+// gives up in one lane gives up in all of them.  The tcgen05.ld / st that
+// follow a wait in the compute warps are warp-collective (.sync.aligned) and
+// must be executed by every lane of the warp or by none.
+TKB_DEVFN bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag));
+}
+
 // The same with a caller-chosen limit (the self-test of the timeout path).
 TKB_DEVFN bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                unsigned long long limit_ns) {
