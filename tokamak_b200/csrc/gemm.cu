@@ -98,7 +98,9 @@ TKB_DEVFN void epi_stage_bias(const GemmParams& p, float* sb, int tn) {
 template <int EPI>
 TKB_DEVFN bool epi_begin(const GemmParams& p, float* sb, int tn, volatile int* abort_flag) {
   if constexpr (EPI == gk::EPI_STORE) {
-    return !*abort_flag;
+    // one decision per warp: the epilogue's tcgen05.ld are warp-collective
+    // (a lane whose wait gave up has raised the flag before voting)
+    return __all_sync(0xffffffffu, !*abort_flag);
   } else {
     // one decision for all 128 epilogue threads (an OR over named barrier 1),
     // taken once every epilogue warp is past the previous tile, so that no
