@@ -67,8 +67,9 @@ typedef struct {
 } TkmRowGeom;
 
 void tkm_row_geom(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *geom);
-/* backward kernel geometry (one chunk per thread for normalisation rows, which
- * keep more state per chunk in the backward) */
+/* backward kernel geometry: the forward's (two chunks per thread for
+ * normalisation rows, column blocks of up to 1024 threads for a twin
+ * epilogue and of up to 256 for other elementwise groups) */
 void tkm_row_geom_bwd(const TkmGraph *g, const PlasmaGroup *pg, int act_bytes, TkmRowGeom *geom);
 int tkm_sm_count_hint(void);
 /* dynamic shared memory of a plasma backward kernel: its two stages of row
