@@ -183,6 +183,11 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
+        if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+            # torchrun sets OMP_NUM_THREADS=1 per rank; rank 0 runs alone here
+            # and takes every host core it may use
+            import oracle
+            oracle.set_num_threads(len(os.sched_getaffinity(0)))
         steps, warm = ref_sample_counts(args)
         v, cores, sample, t = cpu_reference(steps, warm)
         line = {"metric": METRIC, "value": v, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,

@@ -153,3 +153,7 @@ def sgd(p, v, g, lr, momentum=0.9, wd=1e-4, apply_wd=True):
 
 def num_threads():
     return lib().tko_num_threads()
+
+
+def set_num_threads(n):
+    lib().tko_set_num_threads(int(n))

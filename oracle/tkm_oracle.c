@@ -22,6 +22,16 @@ int tko_num_threads(void) {
 #endif
 }
 
+/* threads of the following parallel regions (n >= 1); a launcher may have
+ * set OMP_NUM_THREADS=1 for a process that then times the oracle alone */
+void tko_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n >= 1) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ---------------------------------------------------------------- attention */
 
 /* src/tkm_gpu.cu:302-438.  One (b, q-head, query) row at a time:

@@ -105,6 +105,7 @@ void tko_sgd(float *p, float *v, const float *g, long n, float lr, float momentu
 
 /* Number of OpenMP threads the oracle will use. */
 int tko_num_threads(void);
+void tko_set_num_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -30,3 +30,19 @@ def test_reference_arm_prints_one_contract_line():
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_under_torchrun_runs_on_rank_0_only():
+    """Two ranks as the driver launches them: one line (rank 0), exit 0 for
+    both, and rank 0 times the oracle on every host core it may use although
+    the launcher set OMP_NUM_THREADS=1 per rank."""
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29547", "bench.py", "--impl", "reference",
+           "--gpus", "2", "--steps", "1", "--warmup", "1"]
+    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip().startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2
+    assert d["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
